@@ -1,0 +1,426 @@
+"""Benchmark of the B200 tiny-M FP8 GEMM (driver contract: one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload m9_k6144_n5120]
+
+A "step" is one GEMM Y[M,N] = alpha * X[M,K] . W[N,K]^T over one of R
+rotating (X, W, Y) buffer sets whose total size exceeds 2x the L2 cache, so
+every step reads W cold from HBM (the reference harness's cold-L2 protocol,
+fp8_gemm_task_harness.py:76-96, done by rotation instead of a 256 MiB
+memset).  Inputs are synthetic: X, W ~ N(0,1) FP32, quantised per tensor
+(scale = amax/448, round-to-nearest-even E4M3), as BASELINE.json's configs
+describe.
+
+* value            -- whole-job HBM throughput: algorithmic bytes
+                      (M*K + N*K + 2*M*N, fp8_gemm_task_harness.py:153) of
+                      every step on every rank / max-over-ranks device time.
+* median_us        -- cold-L2 median per-launch latency (CUDA events).
+* cublas_median_us -- torch._scaled_mm (cuBLASLt) on the same buffers and
+                      protocol (the harness's competitor, :68-69), 1 GPU.
+* e2e              -- the same metric through the public API
+                      (candidate_kernel.fp8_gemm) with pinned host inputs:
+                      H2D of X and W, the GEMM, D2H of Y, every step.
+* roofline         -- dominant kernel vs the measured HBM copy bandwidth.
+* cpu_baseline     -- the CPU oracle (oracle/fp8_oracle.reference: dequant +
+                      FP32 matmul + alpha) on this host, rank 0 at N=1.
+
+Multi-GPU (torchrun, one rank per GPU): W is N-sharded (column-parallel);
+each rank computes its [M, N/g] slab with no collective in the timed region
+("scaling": "strong", total work fixed).  The optional BF16 all-gather of Y
+over NCCL is timed separately and reported as allgather_us.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "sm120-fp8-gemm-submit_b200"))
+
+WORKLOADS = {
+    # name: (M, K, N)
+    "m1_k6144_n5120": (1, 6144, 5120),
+    "m9_k6144_n5120": (9, 6144, 5120),
+    "m1_k5120_n8192": (1, 5120, 8192),
+    "m9_k5120_n8192": (9, 5120, 8192),
+    "m1_k5120_n16384": (1, 5120, 16384),
+    "m9_k5120_n16384": (9, 5120, 16384),
+    "m16_k5120_n16384": (16, 5120, 16384),
+}
+DEFAULT_WORKLOAD = "m9_k6144_n5120"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def algo_bytes(m: int, k: int, n: int) -> int:
+    return m * k + n * k + 2 * m * n
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            return {}
+    return {}
+
+
+def committed_traffic(workload: str):
+    """Per-launch DRAM bytes of the dominant kernel from a committed ncu
+    summary (profiles/traffic.json), or None."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        return json.loads(p.read_text()).get(workload)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled while the timed loop runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+            time.sleep(0.15)
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_operands(m, k, n, n_sets, device, seed=0):
+    """N(0,1) FP32 -> per-tensor amax/448 -> E4M3 (torch ops on the device)."""
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def quant(t):
+        s = (t.abs().amax() / 448.0).clamp(min=1e-12)
+        return (t / s).clamp(-448.0, 448.0).to(torch.float8_e4m3fn), s.reshape(1).float()
+
+    sets = []
+    for i in range(n_sets):
+        x32 = torch.randn(m, k, device=device, generator=g)
+        w32 = torch.randn(n, k, device=device, generator=g)
+        x, sx = quant(x32)
+        w, sw = quant(w32)
+        del x32, w32
+        alpha = (sx * sw).float().reshape(1)
+        y = torch.empty(m, n, device=device, dtype=torch.bfloat16)
+        sets.append((x, w, y, sx, sw, alpha))
+    return sets
+
+
+def time_launches(fn, sets, steps, warmup, stream):
+    """Per-launch CUDA-event durations (ms) plus the total span (ms)."""
+    import torch
+
+    for i in range(warmup):
+        fn(sets[i % len(sets)])
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(steps):
+            starts[i].record(stream)
+            fn(sets[i % len(sets)])
+            ends[i].record(stream)
+    torch.cuda.synchronize()
+    per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    return per, starts[0].elapsed_time(ends[-1])
+
+
+def cpu_baseline(m, k, n, budget_s=10.0):
+    """The oracle on this host's cores: a bounded number of full GEMMs."""
+    import numpy as np
+
+    from oracle import fp8_oracle as orc
+
+    try:
+        from threadpoolctl import threadpool_info
+
+        threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:
+        threads = os.cpu_count() or 1
+    xq, wq, sx, sw, alpha = orc.make_case(m, k, n, seed=1, dist="normal")
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter()
+        orc.reference(xq, wq, alpha)
+        times.append(time.perf_counter() - t0)
+        if len(times) >= 200:
+            break
+    med = statistics.median(times)
+    return {"value": algo_bytes(m, k, n) / med / 1e9, "unit": "GB/s", "cores": int(threads),
+            "kind": "port", "median_ms": med * 1e3,
+            "sample": f"{len(times)} full ({m},{k},{n}) GEMMs: numpy LUT dequant + FP32 matmul "
+                      f"+ alpha (oracle/fp8_oracle.reference), median"}
+
+
+def run_reference_arm(args, m, k, n):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    budget = max(3.0, min(20.0, 0.05 * (args.steps + args.warmup)))
+    cb = cpu_baseline(m, k, n, budget_s=budget)
+    line = {
+        "metric": f"achieved HBM GB/s, cold-L2 FP8 GEMM (M={m},K={k},N={n})",
+        "value": round(cb["value"], 3), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(cb["median_ms"], 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": args.workload, "M": m, "K": k, "N": n},
+        "cpu_baseline": {"value": round(cb["value"], 3), "unit": "GB/s", "cores": cb["cores"],
+                         "kind": cb["kind"], "sample": cb["sample"]},
+        "e2e": {"value": round(cb["value"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
+    ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-cublas", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    m, k, n = WORKLOADS[args.workload]
+
+    if args.impl == "reference":
+        run_reference_arm(args, m, k, n)
+        return
+
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=device)
+
+    import candidate_kernel
+    import tinym_b200
+
+    candidate_kernel.build()
+    # This rank's column slab of W (N-sharding); rows rounded to whole tiles.
+    n_local = n // world
+    if n_local * world != n:
+        raise SystemExit(f"N={n} is not divisible by {world} ranks")
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    set_bytes = n_local * k + m * k
+    n_sets = max(2, math.ceil(2.5 * l2 / set_bytes) + 1)
+    sets = make_operands(m, k, n_local, n_sets, device, seed=17 + rank)
+    stream = torch.cuda.current_stream(device)
+    sm_count = torch.cuda.get_device_properties(device).multi_processor_count
+    plan = tinym_b200.select_plan(m, n_local, k, sm_count)
+
+    def ours(s):
+        x, w, y, sx, sw, alpha = s
+        tinym_b200.gemm_ptr(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n_local, k,
+                            alpha_ptr=alpha.data_ptr(), stream=stream.cuda_stream)
+
+    # ---- timed region: K steps, barrier + synchronize on both sides
+    for i in range(args.warmup):
+        ours(sets[i % n_sets])
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        per, span = time_launches(ours, sets, args.steps, 0, stream)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    err = tinym_b200.device_status()
+    if err:
+        raise SystemExit(f"device error word 0x{err:x} after the timed loop")
+
+    span_t = torch.tensor([span], device=device, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(span_t, op=dist.ReduceOp.MAX)
+    span_max = float(span_t.item())
+    total_bytes = algo_bytes(m, k, n_local) * world * args.steps
+    value_gbs = total_bytes / (span_max * 1e-3) / 1e9
+    median_us = statistics.median(per) * 1e3
+    mean_us = statistics.fmean(per) * 1e3
+
+    # optional all-gather of Y (timed separately)
+    allgather_us = None
+    if dist is not None:
+        y_full = torch.empty(world * m * n_local, device=device, dtype=torch.bfloat16)
+        y_loc = sets[0][2].reshape(-1)
+        for _ in range(5):
+            dist.all_gather_into_tensor(y_full, y_loc)
+        torch.cuda.synchronize()
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        evs[0].record()
+        for _ in range(50):
+            dist.all_gather_into_tensor(y_full, y_loc)
+        evs[1].record()
+        torch.cuda.synchronize()
+        t = torch.tensor([evs[0].elapsed_time(evs[1]) / 50 * 1e3], device=device,
+                         dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        allgather_us = float(t.item())
+
+    out = None
+    if rank == 0:
+        peaks = measured_peaks()
+        peak = peaks.get("hbm_gbs")
+        peak_note = "measured" if peak else "fallback"
+        peak = float(peak or FALLBACK_HBM_GBS)
+        achieved = algo_bytes(m, k, n_local) / (mean_us * 1e-6) / 1e9
+        out = {
+            "metric": f"achieved HBM GB/s, cold-L2 FP8 GEMM (M={m},K={k},N={n})",
+            "value": round(value_gbs, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(span_max / args.steps, 6),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "e4m3 in / f32 acc / bf16 out", "data": "synthetic",
+            "config": {"workload": args.workload, "M": m, "K": k, "N": n, "n_per_gpu": n_local,
+                       "parallelism": f"N-sharded x{world}" if world > 1 else "single GPU",
+                       "cold_l2": f"rotation over {n_sets} buffer sets "
+                                  f"({n_sets * set_bytes / 2**20:.0f} MiB > 2x L2 "
+                                  f"{l2 / 2**20:.0f} MiB)",
+                       "plan": plan.as_dict()},
+            "median_us": round(median_us, 3), "mean_us": round(mean_us, 3),
+            "p10_us": round(sorted(per)[len(per) // 10] * 1e3, 3),
+            "p90_us": round(sorted(per)[(9 * len(per)) // 10] * 1e3, 3),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_source": f"{peak_note} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
+                         "traffic": committed_traffic(args.workload),
+                         "algorithmic_bytes_per_launch": algo_bytes(m, k, n_local)},
+            "gpu_launches": args.steps,
+            "clocks": clk.summary(),
+        }
+        if allgather_us is not None:
+            out["allgather_us"] = round(allgather_us, 2)
+
+    # ---- cuBLASLt competitor (1 GPU only, same buffers / protocol)
+    if rank == 0 and world == 1 and not args.no_cublas:
+        def cublas(s):
+            x, w, y, sx, sw, alpha = s
+            torch._scaled_mm(x, w.t(), scale_a=sx, scale_b=sw, out_dtype=torch.bfloat16)
+
+        cb_steps = min(args.steps, 5000)
+        per_cb, _ = time_launches(cublas, sets, cb_steps, args.warmup, stream)
+        out["cublas_median_us"] = round(statistics.median(per_cb) * 1e3, 3)
+        out["speedup_vs_cublas"] = round(out["cublas_median_us"] / median_us, 4)
+
+    # ---- end to end through the public API with host buffers (1 GPU)
+    if world == 1:
+        x, w, y, sx, sw, alpha = sets[0]
+        hx = x.view(torch.uint8).cpu().pin_memory()
+        hw = w.view(torch.uint8).cpu().pin_memory()
+        hy = torch.empty((m, n_local), dtype=torch.bfloat16).pin_memory()
+        dx = torch.empty_like(x.view(torch.uint8))
+        dw = torch.empty_like(w.view(torch.uint8))
+
+        def e2e_step():
+            dx.copy_(hx, non_blocking=True)
+            dw.copy_(hw, non_blocking=True)
+            yy = candidate_kernel.fp8_gemm(dx.view(torch.float8_e4m3fn),
+                                           dw.view(torch.float8_e4m3fn), alpha)
+            hy.copy_(yy, non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+        out["e2e"] = {"value": round(algo_bytes(m, k, n) / (e2e_ms * 1e-3) / 1e9, 3),
+                      "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
+                      "h2d_bytes_per_step": int(hx.numel() + hw.numel()),
+                      "d2h_bytes_per_step": int(hy.numel() * 2),
+                      "api": "candidate_kernel.fp8_gemm"}
+        out["gpu_launches"] = args.steps  # timed region only (one launch per step)
+        if not args.no_cpu_baseline:
+            out["cpu_baseline"] = cpu_baseline(m, k, n, budget_s=args.cpu_budget)
+
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

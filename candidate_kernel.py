@@ -1,0 +1,78 @@
+"""Harness entry point for the B200-native tiny-M FP8 GEMM (drop-in).
+
+Same module name and functions as the reference's candidate_kernel.py
+(``build``, ``prepare_weights``, ``fp8_gemm``; candidate_kernel.py:33-105),
+so ``fp8_gemm_task_harness.py --impl candidate_kernel`` runs unchanged:
+
+    out = fp8_gemm(a, prepare_weights(b), alpha)
+    # a: [M,K] float8_e4m3fn CUDA, b: [N,K] float8_e4m3fn CUDA,
+    # alpha: [1] float32 CUDA  ->  [M,N] bfloat16 CUDA
+
+Differences from the reference adapter:
+
+* ``build()`` loads the in-tree sm_100a libraries (building them with nvcc
+  if they are missing) instead of JIT-compiling for sm_120a.
+* alpha stays on the device: the op reads it inside the kernel, so there is
+  no ``alpha.item()`` synchronisation (reference ``_host_alpha``,
+  candidate_kernel.py:77-94) and the call can be captured in a CUDA graph.
+* any 1 <= M <= 16 and K % 16 == 0 is accepted, not only the six official
+  points (reference src/torch_candidate_extension.cu:40-46).
+
+There is no fallback: if the native library cannot be loaded, ``build()``
+raises.
+"""
+
+from __future__ import annotations
+
+import sys
+import threading
+from pathlib import Path
+from typing import Any
+
+import torch
+
+_ROOT = Path(__file__).resolve().parent
+_SRC = _ROOT / "sm120-fp8-gemm-submit_b200"
+if str(_SRC) not in sys.path:
+    sys.path.insert(0, str(_SRC))
+
+import tinym_b200  # noqa: E402  (package lives in the source root above)
+
+_BUILT = False
+_BUILD_LOCK = threading.Lock()
+_run_alpha_tensor = None
+
+
+def build():
+    """Load (building once if needed) the native op; returns True."""
+    global _BUILT, _run_alpha_tensor
+    if _BUILT:
+        return True
+    with _BUILD_LOCK:
+        if not _BUILT:
+            tinym_b200.load_torch_op()
+            _run_alpha_tensor = torch.ops.sm120_fp8_gemm.run_alpha_tensor
+            _BUILT = True
+    return True
+
+
+def prepare_weights(b: torch.Tensor) -> Any:
+    """Keep the official contiguous [N,K] FP8 layout (reference :68-74)."""
+    if not b.is_cuda or b.dtype != torch.float8_e4m3fn or b.ndim != 2:
+        raise ValueError("B must be a rank-2 CUDA float8_e4m3fn tensor")
+    if not b.is_contiguous():
+        raise ValueError("B must be contiguous row-major")
+    return b
+
+
+def fp8_gemm(a: torch.Tensor, b: torch.Tensor, alpha: torch.Tensor) -> torch.Tensor:
+    """Return (a.float() @ b.float().T) * alpha as BF16 on CUDA."""
+    if not _BUILT:
+        build()
+    if not isinstance(alpha, torch.Tensor) or not alpha.is_cuda or \
+            alpha.dtype != torch.float32 or alpha.numel() != 1:
+        raise ValueError("alpha must be a one-element CUDA float32 tensor")
+    return _run_alpha_tensor(a, b, alpha)
+
+
+__all__ = ["build", "prepare_weights", "fp8_gemm"]

@@ -1,0 +1,137 @@
+/*
+ * tinym_b200.h -- C ABI of the B200 (sm_100a) tiny-M FP8 GEMM.
+ *
+ *     Y[M,N] = bf16( alpha * sum_k X[m,k] * W[n,k] )
+ *
+ * X is [M,K] and W is [N,K], both row-major float8 E4M3 (OCP "e4m3fn"
+ * encoding: no infinities, 0x7F/0xFF are NaN).  Accumulation is FP32 and Y
+ * is row-major BF16 with row stride ldy (>= N) elements.  alpha is the
+ * per-tensor scale product x_scale * w_scale.
+ *
+ * This library replaces the reference's native boundary:
+ *   - the torch op body fp8_gemm_cuda / check_inputs / 6-shape dispatch
+ *     (src/torch_candidate_extension.cu:17-81), and
+ *   - the templated launchers FP8GemmTinyM<...>::run and
+ *     FP8GemmTinyMMmaM16<...>::run with their C-style wrapper
+ *     sm120_tinym_mma_m16_run (include/fp8_gemm_tinym.cuh:724-824).
+ * Unlike those, shapes are runtime values: 1 <= M <= 16, any N >= 1, any
+ * K >= 16 with K % 16 == 0 (TMA row-stride rule).  The dispatch table
+ * (tinym_select_plan) picks the kernel and its tiling per shape.
+ *
+ * Conventions (every entry point):
+ *   - Returns a tinym_status code (0 = TINYM_OK).  No C++ exception ever
+ *     crosses this boundary.  On failure, tinym_last_error() returns a
+ *     message for the calling thread.
+ *   - Launches are asynchronous on the given cudaStream_t (passed as
+ *     void*; NULL = legacy default stream) on the calling thread's current
+ *     CUDA device.  Pointers are device pointers on that device.
+ *   - X and W must be 16-byte aligned; Y must be 2-byte aligned.
+ *   - Inputs are borrowed; nothing is retained after the call returns
+ *     except cached TMA descriptors keyed by (pointer, shape).
+ *   - The library allocates no device memory on the call path.
+ */
+#ifndef TINYM_B200_H
+#define TINYM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TINYM_ABI_VERSION 1
+
+/* Exported-symbol marker (the library is built with hidden visibility). */
+#if defined(__GNUC__)
+#define TINYM_API __attribute__((visibility("default")))
+#else
+#define TINYM_API
+#endif
+
+typedef enum tinym_status {
+    TINYM_OK = 0,
+    TINYM_ERR_INVALID_ARGUMENT = 1, /* null pointer, non-positive size, bad ldy */
+    TINYM_ERR_UNSUPPORTED_SHAPE = 2, /* M outside 1..16 or K % 16 != 0 */
+    TINYM_ERR_MISALIGNED = 3,        /* X/W not 16-byte or Y not 2-byte aligned */
+    TINYM_ERR_CUDA = 4,              /* a CUDA runtime/driver call failed */
+    TINYM_ERR_UNSUPPORTED_DEVICE = 5,/* current device is not sm_100 */
+    TINYM_ERR_DEVICE_TIMEOUT = 6,    /* a bounded device-side wait expired */
+    TINYM_ERR_BAD_PLAN = 7           /* an explicit plan is inconsistent */
+} tinym_status;
+
+/* Kernel families (tinym_plan.kernel). */
+#define TINYM_KERNEL_TC 1      /* tcgen05 swap-AB: W tile = MMA A (M=128), X = MMA B */
+#define TINYM_KERNEL_SIMT_M1 2 /* M == 1 only: CUDA-core dequantise + FP32 FMA */
+
+/* A launch plan: which kernel and how the problem is cut.  Produced by
+ * tinym_select_plan (the shape-dispatch table, replacing the hard-coded
+ * six-way template dispatch of src/torch_candidate_extension.cu:60-78) and
+ * accepted back by tinym_fp8_gemm_plan for sweeps. */
+typedef struct tinym_plan {
+    int32_t kernel;         /* TINYM_KERNEL_* */
+    int32_t split_k;        /* CTAs per 128-row W tile (K split, 1..8); >1 => cluster of split_k CTAs */
+    int32_t stages;         /* shared-memory ring depth (W+X stages) */
+    int32_t mma_n;          /* TC: MMA N (8 or 16, >= M); SIMT: 0 */
+    int32_t consumer_warps; /* SIMT: dequant/FMA warps (4 or 8); TC: 0 */
+    int32_t block_k;        /* K bytes per stage (128) */
+    int32_t tiles_n;        /* out: ceil(N / 128) */
+    int32_t grid_ctas;      /* out: CTAs launched = tiles_n * split_k */
+    int32_t smem_bytes;     /* out: dynamic shared memory per CTA */
+    int32_t threads;        /* out: threads per CTA */
+} tinym_plan;
+
+/* Y = (x_scale * w_scale) * X . W^T.  Mirrors FP8GemmTinyM::run /
+ * FP8GemmTinyMMmaM16::run (include/fp8_gemm_tinym.cuh:514-518,314-318):
+ * same operands, same scale pair, same stream argument. */
+TINYM_API int tinym_fp8_gemm(const void* x, const void* w, void* y,
+                   int64_t m, int64_t n, int64_t k,
+                   float x_scale, float w_scale, void* stream);
+
+/* As tinym_fp8_gemm, but alpha is read on the device from alpha_dev (one
+ * FP32 value) when the kernel runs, so no host synchronisation is needed to
+ * obtain it.  Replaces the torch op run(Tensor a, Tensor b, float alpha)
+ * plus the adapter's alpha.item() cache (candidate_kernel.py:77-102). */
+TINYM_API int tinym_fp8_gemm_dev_alpha(const void* x, const void* w, void* y,
+                             int64_t m, int64_t n, int64_t k,
+                             const float* alpha_dev, void* stream);
+
+/* Full form: explicit output row stride, alpha either on the device
+ * (alpha_dev != NULL) or by value, and an optional plan (NULL = use the
+ * dispatch table).  Used by the N-sharded wrapper (writes its column slab
+ * of a wider Y) and by tuning sweeps.  No reference counterpart beyond the
+ * launchers above. */
+TINYM_API int tinym_fp8_gemm_ex(const void* x, const void* w, void* y, int64_t ldy,
+                      int64_t m, int64_t n, int64_t k,
+                      const float* alpha_dev, float alpha,
+                      const tinym_plan* plan, void* stream);
+
+/* The shape-dispatch table: fills *out with the plan tinym_fp8_gemm would
+ * use for (m, n, k) on a GPU with sm_count SMs.  Host-only logic (needs no
+ * GPU).  Replaces src/torch_candidate_extension.cu:40-46,60-78. */
+TINYM_API int tinym_select_plan(int64_t m, int64_t n, int64_t k, int32_t sm_count,
+                      tinym_plan* out);
+
+/* Validate a plan for (m, n, k) and fill its derived fields.  Host-only. */
+TINYM_API int tinym_check_plan(int64_t m, int64_t n, int64_t k, tinym_plan* plan);
+
+/* Device error word of the current device: bit flags set by kernels whose
+ * bounded waits expired (0 = none).  Synchronises the device.  clear != 0
+ * resets the word.  The reference has no counterpart (its waits spin
+ * forever, include/fp8_gemm_tinym.cuh:164-176). */
+TINYM_API int tinym_device_status(uint32_t* flags, int32_t clear);
+
+/* Human-readable name of a tinym_status code (static string). */
+TINYM_API const char* tinym_status_string(int32_t status);
+
+/* Message for the last failing call on this thread ("" if none). */
+TINYM_API const char* tinym_last_error(void);
+
+/* TINYM_ABI_VERSION of the loaded library. */
+TINYM_API int32_t tinym_abi_version(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* TINYM_B200_H */

@@ -1,0 +1,426 @@
+// tinym_capi.cu -- host launcher, shape-dispatch table and C ABI.
+//
+// Replaces the reference's launch plumbing (include/fp8_gemm_tinym.cuh:
+// 79-132 tensor-map encoding, 724-808 ::run, 810-824 the cudaError_t
+// wrapper) and the shape gate / template dispatch of
+// src/torch_candidate_extension.cu:33-81.  Differences that matter on B200:
+//   * shapes are runtime values and the dispatch table is a function of
+//     (M, N, K, SM count) instead of six hard-coded template instances;
+//   * TMA descriptors are cached per (pointer, shape) instead of being
+//     re-encoded on every call (reference :742-755, :794-799), and the
+//     shared-memory attribute is set once per device (reference :769-770);
+//   * alpha may stay on the device (no host synchronisation);
+//   * errors come back as status codes with a per-thread message, never as
+//     exceptions.
+// cuTensorMapEncodeTiled is fetched through cudaGetDriverEntryPoint, so the
+// library links only the static CUDA runtime and loads on machines without
+// a GPU driver (its entry points then return TINYM_ERR_CUDA).
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/tinym_b200.h"
+#include "tinym_kernels.cuh"
+
+namespace {
+
+using tinym::kBlockK;
+using tinym::kTcThreads;
+using tinym::kTileRows;
+using tinym::TinymParams;
+
+constexpr int kMaxDevices = 64;
+constexpr int kMaxSplit = 8;       // portable cluster size
+constexpr int kMaxStages = 12;
+constexpr int kSmemLimit = 232448; // 227 KiB opt-in per CTA on sm_100
+constexpr uint64_t kDefaultTimeoutNs = 1000000000ull;  // 1 s per wait
+
+thread_local char t_last_error[512] = "";
+
+int fail(int status, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+    va_end(ap);
+    return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(TINYM_ERR_CUDA, "%s failed: %s (%s)", what, cudaGetErrorName(e),
+                cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------- driver entry point
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+cudaError_t g_encode_err = cudaSuccess;
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        g_encode_err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+        if (g_encode_err == cudaSuccess && q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    return g_encode;
+}
+
+// ---------------------------------------------------------------- per-device state
+struct DeviceInfo {
+    std::atomic<int> ready{0};
+    int sm_count = 0;
+    int cc_major = 0, cc_minor = 0;
+    std::atomic<uint32_t> attr_done{0};  // bit per kernel instance: smem attribute set
+};
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int device_info(int dev, DeviceInfo** out) {
+    if (dev < 0 || dev >= kMaxDevices) return fail(TINYM_ERR_CUDA, "device ordinal %d out of range", dev);
+    DeviceInfo& d = g_dev[dev];
+    if (!d.ready.load(std::memory_order_acquire)) {
+        std::lock_guard<std::mutex> lk(g_dev_mu);
+        if (!d.ready.load(std::memory_order_relaxed)) {
+            cudaError_t e;
+            if ((e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+                return cuda_fail(e, "cudaDeviceGetAttribute(MultiProcessorCount)");
+            if ((e = cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess)
+                return cuda_fail(e, "cudaDeviceGetAttribute(ComputeCapabilityMajor)");
+            if ((e = cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess)
+                return cuda_fail(e, "cudaDeviceGetAttribute(ComputeCapabilityMinor)");
+            d.ready.store(1, std::memory_order_release);
+        }
+    }
+    if (d.cc_major != 10 || d.cc_minor != 0)
+        return fail(TINYM_ERR_UNSUPPORTED_DEVICE,
+                    "device %d is sm_%d%d; this library is built for sm_100a (B200)", dev,
+                    d.cc_major, d.cc_minor);
+    *out = &d;
+    return TINYM_OK;
+}
+
+// ---------------------------------------------------------------- tensor-map cache
+struct MapKey {
+    const void* ptr;
+    int64_t rows, cols;
+    int32_t box_rows, swizzle, dev;
+    bool operator==(const MapKey& o) const {
+        return ptr == o.ptr && rows == o.rows && cols == o.cols && box_rows == o.box_rows &&
+               swizzle == o.swizzle && dev == o.dev;
+    }
+};
+struct MapEntry {
+    MapKey key;
+    alignas(64) CUtensorMap map;
+    uint64_t stamp;
+    bool used;
+};
+constexpr int kMapCacheSize = 256;
+MapEntry g_maps[kMapCacheSize];
+uint64_t g_map_clock = 0;
+std::mutex g_map_mu;
+
+// Encodes (or fetches) the map of a row-major [rows, cols] uint8 matrix read
+// in boxes of [box_rows, 128 bytes]; swizzle 1 = 128B, 0 = none.
+int get_map(const void* ptr, int64_t rows, int64_t cols, int box_rows, int swizzle, int dev,
+            CUtensorMap* out) {
+    const MapKey key{ptr, rows, cols, box_rows, swizzle, dev};
+    std::lock_guard<std::mutex> lk(g_map_mu);
+    MapEntry* victim = &g_maps[0];
+    for (auto& e : g_maps) {
+        if (e.used && e.key == key) {
+            e.stamp = ++g_map_clock;
+            *out = e.map;
+            return TINYM_OK;
+        }
+        if (!e.used || e.stamp < victim->stamp) victim = &e;
+        if (!victim->used) break;
+    }
+    auto encode = get_encode();
+    if (!encode)
+        return fail(TINYM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (%s)",
+                    cudaGetErrorString(g_encode_err));
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(kBlockK), static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t estr[2] = {1, 1};
+    CUtensorMap map;
+    CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(TINYM_ERR_CUDA,
+                    "cuTensorMapEncodeTiled failed (CUresult %d) for [%lld x %lld] box %d rows",
+                    static_cast<int>(r), static_cast<long long>(rows),
+                    static_cast<long long>(cols), box_rows);
+    victim->key = key;
+    victim->map = map;
+    victim->stamp = ++g_map_clock;
+    victim->used = true;
+    *out = map;
+    return TINYM_OK;
+}
+
+// ---------------------------------------------------------------- plans
+int x_stage_bytes(const tinym_plan& p) {
+    return p.kernel == TINYM_KERNEL_TC ? p.mma_n * kBlockK : kBlockK;
+}
+
+int fill_derived(int64_t m, int64_t n, int64_t k, tinym_plan* p) {
+    const int64_t tiles = (n + kTileRows - 1) / kTileRows;
+    const int64_t kb = (k + kBlockK - 1) / kBlockK;
+    if (p->kernel != TINYM_KERNEL_TC && p->kernel != TINYM_KERNEL_SIMT_M1)
+        return fail(TINYM_ERR_BAD_PLAN, "plan.kernel %d is not a kernel family", p->kernel);
+    if (p->block_k != kBlockK) return fail(TINYM_ERR_BAD_PLAN, "plan.block_k must be %d", kBlockK);
+    if (p->kernel == TINYM_KERNEL_TC) {
+        if (p->mma_n != 8 && p->mma_n != 16)
+            return fail(TINYM_ERR_BAD_PLAN, "plan.mma_n must be 8 or 16");
+        if (p->mma_n < m) return fail(TINYM_ERR_BAD_PLAN, "plan.mma_n %d < M %lld", p->mma_n, (long long)m);
+        p->consumer_warps = 0;
+        p->threads = kTcThreads;
+    } else {
+        if (m != 1) return fail(TINYM_ERR_BAD_PLAN, "the SIMT kernel handles M == 1 only");
+        if (p->consumer_warps != 4 && p->consumer_warps != 8)
+            return fail(TINYM_ERR_BAD_PLAN, "plan.consumer_warps must be 4 or 8");
+        p->mma_n = 0;
+        p->threads = 32 * (p->consumer_warps + 1);
+    }
+    if (p->split_k < 1 || p->split_k > kMaxSplit)
+        return fail(TINYM_ERR_BAD_PLAN, "plan.split_k must be in 1..%d", kMaxSplit);
+    const int64_t per = (kb + p->split_k - 1) / p->split_k;
+    if ((p->split_k - 1) * per >= kb)
+        return fail(TINYM_ERR_BAD_PLAN, "split_k %d leaves an empty K range (K blocks %lld)",
+                    p->split_k, (long long)kb);
+    if (p->stages < 2 || p->stages > kMaxStages)
+        return fail(TINYM_ERR_BAD_PLAN, "plan.stages must be in 2..%d", kMaxStages);
+    if (tiles > 65535) return fail(TINYM_ERR_UNSUPPORTED_SHAPE, "N too large (%lld tiles)", (long long)tiles);
+    const tinym::SmemLayout L = tinym::smem_layout(p->stages, x_stage_bytes(*p), p->split_k,
+                                                   static_cast<int>(m));
+    if (L.bytes > static_cast<uint32_t>(kSmemLimit))
+        return fail(TINYM_ERR_BAD_PLAN, "plan needs %u bytes of shared memory (> %d)", L.bytes,
+                    kSmemLimit);
+    p->tiles_n = static_cast<int32_t>(tiles);
+    p->grid_ctas = static_cast<int32_t>(tiles * p->split_k);
+    p->smem_bytes = static_cast<int32_t>(L.bytes);
+    return TINYM_OK;
+}
+
+int check_shape(int64_t m, int64_t n, int64_t k) {
+    if (m < 1 || n < 1 || k < 1)
+        return fail(TINYM_ERR_INVALID_ARGUMENT, "M, N, K must be positive (got %lld, %lld, %lld)",
+                    (long long)m, (long long)n, (long long)k);
+    if (m > 16)
+        return fail(TINYM_ERR_UNSUPPORTED_SHAPE, "unsupported shape M=%lld, K=%lld, N=%lld: M must be <= 16",
+                    (long long)m, (long long)k, (long long)n);
+    if (k % 16 != 0)
+        return fail(TINYM_ERR_UNSUPPORTED_SHAPE,
+                    "unsupported shape M=%lld, K=%lld, N=%lld: K must be a multiple of 16",
+                    (long long)m, (long long)k, (long long)n);
+    if (k > (int64_t(1) << 31) - 1024 || n > (int64_t(1) << 31) - 1)
+        return fail(TINYM_ERR_UNSUPPORTED_SHAPE, "K or N exceeds the 32-bit index range");
+    return TINYM_OK;
+}
+
+// Heuristic part of the dispatch table: the largest K split (cluster size)
+// that keeps every (tile, split) CTA in one wave of sm_count CTAs, leaves
+// every CTA at least 2 K blocks, and stays within the portable cluster size.
+int heuristic_split(int64_t tiles, int64_t kb, int sm_count) {
+    int best = 1;
+    for (int s = 2; s <= kMaxSplit; ++s) {
+        if (tiles * s > sm_count) break;
+        const int64_t per = (kb + s - 1) / s;
+        if (per < 2 || (s - 1) * per >= kb) continue;
+        best = s;
+    }
+    return best;
+}
+
+int max_stages_fitting(const tinym_plan& p, int64_t m) {
+    int st = kMaxStages;
+    while (st > 2) {
+        tinym_plan q = p;
+        q.stages = st;
+        if (tinym::smem_layout(st, x_stage_bytes(q), q.split_k, static_cast<int>(m)).bytes <=
+            static_cast<uint32_t>(kSmemLimit))
+            break;
+        --st;
+    }
+    return st;
+}
+
+}  // namespace
+
+// =====================================================================
+// C ABI
+// =====================================================================
+extern "C" {
+
+int32_t tinym_abi_version(void) { return TINYM_ABI_VERSION; }
+
+const char* tinym_last_error(void) { return t_last_error; }
+
+const char* tinym_status_string(int32_t status) {
+    switch (status) {
+        case TINYM_OK: return "TINYM_OK";
+        case TINYM_ERR_INVALID_ARGUMENT: return "TINYM_ERR_INVALID_ARGUMENT";
+        case TINYM_ERR_UNSUPPORTED_SHAPE: return "TINYM_ERR_UNSUPPORTED_SHAPE";
+        case TINYM_ERR_MISALIGNED: return "TINYM_ERR_MISALIGNED";
+        case TINYM_ERR_CUDA: return "TINYM_ERR_CUDA";
+        case TINYM_ERR_UNSUPPORTED_DEVICE: return "TINYM_ERR_UNSUPPORTED_DEVICE";
+        case TINYM_ERR_DEVICE_TIMEOUT: return "TINYM_ERR_DEVICE_TIMEOUT";
+        case TINYM_ERR_BAD_PLAN: return "TINYM_ERR_BAD_PLAN";
+        default: return "TINYM_ERR_UNKNOWN";
+    }
+}
+
+int tinym_check_plan(int64_t m, int64_t n, int64_t k, tinym_plan* plan) {
+    t_last_error[0] = '\0';
+    if (!plan) return fail(TINYM_ERR_INVALID_ARGUMENT, "plan is NULL");
+    int st = check_shape(m, n, k);
+    if (st != TINYM_OK) return st;
+    return fill_derived(m, n, k, plan);
+}
+
+int tinym_select_plan(int64_t m, int64_t n, int64_t k, int32_t sm_count, tinym_plan* out) {
+    t_last_error[0] = '\0';
+    if (!out) return fail(TINYM_ERR_INVALID_ARGUMENT, "out is NULL");
+    if (sm_count < 1) return fail(TINYM_ERR_INVALID_ARGUMENT, "sm_count must be positive");
+    int st = check_shape(m, n, k);
+    if (st != TINYM_OK) return st;
+    const int64_t tiles = (n + kTileRows - 1) / kTileRows;
+    const int64_t kb = (k + kBlockK - 1) / kBlockK;
+    tinym_plan p{};
+    p.kernel = TINYM_KERNEL_TC;
+    p.mma_n = m <= 8 ? 8 : 16;
+    p.block_k = kBlockK;
+    p.split_k = heuristic_split(tiles, kb, sm_count);
+    p.stages = 2;
+    p.stages = std::min<int64_t>(max_stages_fitting(p, m), std::max<int64_t>(2, (kb + p.split_k - 1) / p.split_k));
+    *out = p;
+    return fill_derived(m, n, k, out);
+}
+
+int tinym_fp8_gemm_ex(const void* x, const void* w, void* y, int64_t ldy, int64_t m, int64_t n,
+                      int64_t k, const float* alpha_dev, float alpha, const tinym_plan* plan,
+                      void* stream) {
+    t_last_error[0] = '\0';
+    if (!x || !w || !y) return fail(TINYM_ERR_INVALID_ARGUMENT, "X, W and Y must be non-null");
+    int st = check_shape(m, n, k);
+    if (st != TINYM_OK) return st;
+    if (ldy < n) return fail(TINYM_ERR_INVALID_ARGUMENT, "ldy (%lld) < N (%lld)", (long long)ldy, (long long)n);
+    if (ldy > (int64_t(1) << 31) - 1) return fail(TINYM_ERR_UNSUPPORTED_SHAPE, "ldy exceeds the 32-bit range");
+    if ((reinterpret_cast<uintptr_t>(x) & 15u) || (reinterpret_cast<uintptr_t>(w) & 15u))
+        return fail(TINYM_ERR_MISALIGNED, "X and W must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(y) & 1u) return fail(TINYM_ERR_MISALIGNED, "Y must be 2-byte aligned");
+    if (!alpha_dev && !std::isfinite(alpha)) return fail(TINYM_ERR_INVALID_ARGUMENT, "alpha must be finite");
+
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    DeviceInfo* di = nullptr;
+    if ((st = device_info(dev, &di)) != TINYM_OK) return st;
+
+    tinym_plan p{};
+    if (plan) {
+        p = *plan;
+        if ((st = fill_derived(m, n, k, &p)) != TINYM_OK) return st;
+    } else if ((st = tinym_select_plan(m, n, k, di->sm_count, &p)) != TINYM_OK) {
+        return st;
+    }
+
+    CUtensorMap tm_w, tm_x;
+    if ((st = get_map(w, n, k, kTileRows, 1, dev, &tm_w)) != TINYM_OK) return st;
+    if (p.kernel == TINYM_KERNEL_TC) {
+        if ((st = get_map(x, m, k, p.mma_n, 1, dev, &tm_x)) != TINYM_OK) return st;
+    } else {
+        if ((st = get_map(x, m, k, 1, 0, dev, &tm_x)) != TINYM_OK) return st;
+    }
+
+    TinymParams prm{};
+    prm.y = static_cast<__nv_bfloat16*>(y);
+    prm.alpha_ptr = alpha_dev;
+    prm.alpha = alpha;
+    prm.m = static_cast<int32_t>(m);
+    prm.n = static_cast<int32_t>(n);
+    prm.k = static_cast<int32_t>(k);
+    prm.ldy = static_cast<int32_t>(ldy);
+    prm.kb_total = static_cast<int32_t>((k + kBlockK - 1) / kBlockK);
+    prm.kb_per_split = (prm.kb_total + p.split_k - 1) / p.split_k;
+    prm.split = p.split_k;
+    prm.stages = p.stages;
+    prm.timeout_ns = kDefaultTimeoutNs;
+
+    const void* fn = nullptr;
+    uint32_t attr_bit = 0;
+    if (p.kernel == TINYM_KERNEL_TC) {
+        fn = p.mma_n == 8 ? reinterpret_cast<const void*>(&tinym::tinym_tc_kernel<8>)
+                          : reinterpret_cast<const void*>(&tinym::tinym_tc_kernel<16>);
+        attr_bit = p.mma_n == 8 ? 1u : 2u;
+    } else {
+        fn = p.consumer_warps == 4 ? reinterpret_cast<const void*>(&tinym::tinym_simt_m1_kernel<4>)
+                                   : reinterpret_cast<const void*>(&tinym::tinym_simt_m1_kernel<8>);
+        attr_bit = p.consumer_warps == 4 ? 4u : 8u;
+    }
+    if (!(di->attr_done.load(std::memory_order_acquire) & attr_bit)) {
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
+        di->attr_done.fetch_or(attr_bit, std::memory_order_acq_rel);
+    }
+
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(p.split_k), static_cast<unsigned>(p.tiles_n), 1);
+    cfg.blockDim = dim3(static_cast<unsigned>(p.threads), 1, 1);
+    cfg.dynamicSmemBytes = static_cast<size_t>(p.smem_bytes);
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attrs[1];
+    cfg.numAttrs = 0;
+    if (p.split_k > 1) {
+        attrs[0].id = cudaLaunchAttributeClusterDimension;
+        attrs[0].val.clusterDim.x = static_cast<unsigned>(p.split_k);
+        attrs[0].val.clusterDim.y = 1;
+        attrs[0].val.clusterDim.z = 1;
+        cfg.attrs = attrs;
+        cfg.numAttrs = 1;
+    }
+    void* args[3] = {&tm_w, &tm_x, &prm};
+    e = cudaLaunchKernelExC(&cfg, fn, args);
+    if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
+    return TINYM_OK;
+}
+
+int tinym_fp8_gemm(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k,
+                   float x_scale, float w_scale, void* stream) {
+    return tinym_fp8_gemm_ex(x, w, y, n, m, n, k, nullptr, x_scale * w_scale, nullptr, stream);
+}
+
+int tinym_fp8_gemm_dev_alpha(const void* x, const void* w, void* y, int64_t m, int64_t n,
+                             int64_t k, const float* alpha_dev, void* stream) {
+    if (!alpha_dev) return fail(TINYM_ERR_INVALID_ARGUMENT, "alpha_dev must be non-null");
+    return tinym_fp8_gemm_ex(x, w, y, n, m, n, k, alpha_dev, 0.0f, nullptr, stream);
+}
+
+int tinym_device_status(uint32_t* flags, int32_t clear) {
+    t_last_error[0] = '\0';
+    if (!flags) return fail(TINYM_ERR_INVALID_ARGUMENT, "flags is NULL");
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+    e = cudaMemcpyFromSymbol(flags, tinym::g_err_word, sizeof(uint32_t));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyFromSymbol(error word)");
+    if (clear) {
+        const uint32_t zero = 0;
+        e = cudaMemcpyToSymbol(tinym::g_err_word, &zero, sizeof(uint32_t));
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyToSymbol(error word)");
+    }
+    return *flags ? fail(TINYM_ERR_DEVICE_TIMEOUT, "device error word 0x%x", *flags) : TINYM_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,453 @@
+// tinym_kernels.cuh -- sm_100a kernels of the tiny-M FP8 GEMM.
+//
+//   Y[m, n] = bf16( alpha * sum_k X[m,k] * W[n,k] ),  1 <= M <= 16.
+//
+// The work is cut into 128-row W tiles ("tiles", blockIdx.y) and, when the
+// tiles alone cannot fill the GPU, into split_k contiguous K ranges
+// (blockIdx.x).  The split_k CTAs of one tile form a thread-block cluster and
+// reduce their FP32 partial sums through distributed shared memory into the
+// cluster's rank-0 CTA, which applies alpha and writes BF16 -- a
+// deterministic, single-launch split-K with no global scratch memory.
+//
+// Two consumers share this skeleton:
+//
+//  * tinym_tc_kernel<MMA_N> ("swap-AB"): the W tile [128 x 128 B] is the A
+//    operand of tcgen05.mma.kind::f8f6f4 (MMA M = 128) and X, padded by TMA
+//    zero fill to MMA_N (8 or 16) rows, is the B operand.  The accumulator
+//    D[128 x MMA_N] (FP32) lives in tensor memory; four epilogue warps read
+//    it with tcgen05.ld.  Replaces the reference's M<=16 mma.sync kernel
+//    (include/fp8_gemm_tinym.cuh:321-461), whose m16n8k32 warp MMA put M on
+//    the MMA's M side.
+//
+//  * tinym_simt_m1_kernel<CWARPS>: M = 1 only.  Consumer warps widen the
+//    E4M3 W bytes to FP32 and FMA them against X on the CUDA cores; eight
+//    lanes share one W row (one 16-byte chunk each) and are reduced with
+//    warp shuffles.  The M=1 counterpart of the reference's scalar kernel
+//    (include/fp8_gemm_tinym.cuh:521-722).
+//
+// Both stream W with 2-D TMA boxes of 128 rows x 128 bytes using the
+// 128-byte swizzle into a ring of `stages` shared-memory slots guarded by
+// full/empty mbarriers.  Every wait is bounded (WaitGuard): a wait that runs
+// out sets a bit in the device error word and the CTA drains what it has in
+// flight, frees its tensor memory and exits.
+#pragma once
+
+#include "tinym_ptx.cuh"
+
+namespace tinym {
+
+// Device error word (one per device; read by tinym_device_status).
+__device__ uint32_t g_err_word;
+
+enum : uint32_t {
+    kErrProducerWait = 1u << 0,
+    kErrMmaWait = 1u << 1,
+    kErrEpilogueWait = 1u << 2,
+    kErrDrain = 1u << 3,
+    kErrConsumerWait = 1u << 4,
+};
+
+constexpr int kTileRows = 128;   // W rows per tile (= MMA M)
+constexpr int kBlockK = 128;     // K bytes per stage (= one 128B swizzle row)
+constexpr int kWStageBytes = kTileRows * kBlockK;  // 16 KiB
+constexpr int kTcThreads = 192;  // warp0 TMA, warp1 MMA, warps2-5 epilogue
+constexpr int kTmemCols = 32;    // minimum allocation; MMA_N <= 16 columns used
+
+struct TinymParams {
+    __nv_bfloat16* y;
+    const float* alpha_ptr;  // if non-null, alpha is read here on the device
+    float alpha;
+    int32_t m, n, k, ldy;
+    int32_t kb_total;      // ceil(K / 128)
+    int32_t kb_per_split;  // K blocks per CTA (last CTA of a cluster may get fewer)
+    int32_t split;         // CTAs per tile (cluster size along x)
+    int32_t stages;
+    uint64_t timeout_ns;
+};
+
+// Shared-memory carve-up, identical on host (size) and device (offsets).
+struct SmemLayout {
+    uint32_t w_off, x_off, red_off, bar_off, misc_off, bytes;
+};
+
+__host__ __device__ inline SmemLayout smem_layout(int stages, int x_stage_bytes, int split,
+                                                  int m) {
+    SmemLayout L;
+    L.w_off = 0;
+    L.x_off = L.w_off + static_cast<uint32_t>(stages) * kWStageBytes;
+    L.red_off = L.x_off + static_cast<uint32_t>(stages * x_stage_bytes);
+    L.red_off = (L.red_off + 15u) & ~15u;
+    const uint32_t red_bytes = static_cast<uint32_t>((split - 1) * m * kTileRows * 4);
+    L.bar_off = (L.red_off + red_bytes + 7u) & ~7u;
+    L.misc_off = L.bar_off + static_cast<uint32_t>(2 * stages + 1) * 8u;
+    // +1024: the dynamic window is re-aligned to 1024 bytes in the kernel.
+    L.bytes = L.misc_off + 16u + 1024u;
+    return L;
+}
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+    const uint32_t a = smem_u32(p);
+    return p + (((a + 1023u) & ~1023u) - a);
+}
+
+// Output for one W row n of the tile: either stored (split == 1), pushed to
+// the cluster leader (rank > 0), or kept for the leader's reduction.
+__device__ __forceinline__ float load_alpha(const TinymParams& p) {
+    return p.alpha_ptr ? __ldg(p.alpha_ptr) : p.alpha;
+}
+
+// =====================================================================
+// tcgen05 swap-AB kernel
+// =====================================================================
+template <int MMA_N>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tinym_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
+                    const __grid_constant__ CUtensorMap tm_x, const TinymParams p) {
+    static_assert(MMA_N == 8 || MMA_N == 16, "MMA_N must be 8 or 16");
+    constexpr int kXStageBytes = MMA_N * kBlockK;  // 1 or 2 KiB, 1024-aligned
+    constexpr uint32_t kStageTx = kWStageBytes + kXStageBytes;
+    constexpr uint32_t kIdesc = idesc_e4m3_f32(kTileRows, MMA_N);
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = align1024(smem_raw);
+    const SmemLayout L = smem_layout(p.stages, kXStageBytes, p.split, p.m);
+    const uint32_t s_base = smem_u32(smem);
+    const uint32_t w_ring = s_base + L.w_off;
+    const uint32_t x_ring = s_base + L.x_off;
+    const uint32_t bars = s_base + L.bar_off;
+    const int stages = p.stages;
+    auto full_bar = [&](int s) { return bars + 8u * s; };
+    auto empty_bar = [&](int s) { return bars + 8u * (stages + s); };
+    const uint32_t acc_bar = bars + 8u * (2 * stages);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.misc_off);
+    volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L.misc_off + 4);
+    float* red = reinterpret_cast<float*>(smem + L.red_off);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int split_idx = blockIdx.x;
+    const int tile = blockIdx.y;
+    const int kb0 = split_idx * p.kb_per_split;
+    const int kb1 = min(kb0 + p.kb_per_split, p.kb_total);
+    const int nkb = kb1 - kb0;  // >= 1 by construction of the plan
+
+    const WaitGuard guard{abort_flag, &g_err_word, p.timeout_ns};
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        mbar_init(acc_bar, 1);
+        *abort_flag = 0u;
+        fence_mbar_init();
+        fence_proxy_async_smem();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tm_w);
+        tma_prefetch_desc(&tm_x);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before_sync();
+    __syncthreads();
+    tc_fence_after_sync();
+    const uint32_t tmem_d = *tmem_slot;
+    // Cluster phase 1: every CTA of the cluster has started (and set up its
+    // shared memory) before any CTA writes into another's shared memory.
+    if (p.split > 1) cluster_arrive_relaxed();
+
+    float acc[MMA_N];
+    bool have_acc = false;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer
+            const uint64_t pol_w = l2_policy_evict_first();
+            const uint64_t pol_x = l2_policy_evict_last();
+            int issued = 0;
+            for (int i = 0; i < nkb; ++i) {
+                const int s = i % stages;
+                if (i >= stages) {
+                    if (!mbar_wait(empty_bar(s), ((i / stages) - 1) & 1, guard, kErrProducerWait))
+                        break;
+                }
+                const int kc = (kb0 + i) * kBlockK;
+                mbar_expect_tx(full_bar(s), kStageTx);
+                tma_load_2d(w_ring + s * kWStageBytes, &tm_w, full_bar(s), kc, tile * kTileRows,
+                            pol_w);
+                tma_load_2d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), kc, 0, pol_x);
+                ++issued;
+            }
+            if (*abort_flag) {
+                // Drain the copies still in flight before shared memory is released.
+                for (int j = max(0, issued - stages); j < issued; ++j)
+                    mbar_drain(full_bar(j % stages), (j / stages) & 1, guard, kErrDrain);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer (one thread)
+            for (int i = 0; i < nkb; ++i) {
+                const int s = i % stages;
+                if (!mbar_wait(full_bar(s), (i / stages) & 1, guard, kErrMmaWait)) break;
+                tc_fence_after_sync();
+                const uint32_t a0 = w_ring + s * kWStageBytes;
+                const uint32_t b0 = x_ring + s * kXStageBytes;
+#pragma unroll
+                for (int kk = 0; kk < kBlockK / 32; ++kk) {
+                    umma_e4m3(tmem_d, sw128_kmajor_desc(a0 + kk * 32),
+                              sw128_kmajor_desc(b0 + kk * 32), kIdesc,
+                              (i > 0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit(empty_bar(s));  // frees the slot once these MMAs retire
+            }
+            umma_commit(acc_bar);  // accumulator complete (or all issued MMAs retired)
+            if (*abort_flag) mbar_drain(acc_bar, 0, guard, kErrDrain);
+        }
+    } else {
+        // ---------------- epilogue warps 2..5: TMEM lanes 32*(warp%4) ..
+        // tcgen05.ld is .sync.aligned: the whole warp takes the same branch.
+        const bool ready = mbar_wait(acc_bar, 0, guard, kErrEpilogueWait) && !*abort_flag;
+        if (__all_sync(0xFFFFFFFFu, ready)) {
+            tc_fence_after_sync();
+            const uint32_t taddr = tmem_d + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+            if constexpr (MMA_N == 8) {
+                tmem_ld_x8(taddr, acc);
+            } else {
+                tmem_ld_x16(taddr, acc);
+            }
+            have_acc = true;
+        }
+    }
+    __syncwarp();
+
+    // ---------------- output / split-K reduction
+    const int row = (warp & 3) * 32 + lane;  // W row within the tile (epilogue warps)
+    const int n_idx = tile * kTileRows + row;
+    if (p.split == 1) {
+        if (have_acc && n_idx < p.n) {
+            const float alpha = load_alpha(p);
+#pragma unroll
+            for (int m = 0; m < MMA_N; ++m)
+                if (m < p.m) p.y[static_cast<size_t>(m) * p.ldy + n_idx] = __float2bfloat16_rn(acc[m] * alpha);
+        }
+    } else {
+        __syncwarp();
+        cluster_wait_acquire();  // phase 1 complete: all CTAs of the cluster are resident
+        if (have_acc && split_idx > 0) {
+            const uint32_t remote = dsmem_map(smem_u32(red), 0);
+#pragma unroll
+            for (int m = 0; m < MMA_N; ++m)
+                if (m < p.m)
+                    dsmem_st_f32(remote + 4u * (((split_idx - 1) * p.m + m) * kTileRows + row),
+                                 acc[m]);
+        }
+        __syncwarp();
+        cluster_arrive_release();  // phase 2: partial sums are in the leader's shared memory
+        cluster_wait_acquire();
+        if (have_acc && split_idx == 0 && n_idx < p.n) {
+            const float alpha = load_alpha(p);
+#pragma unroll
+            for (int m = 0; m < MMA_N; ++m) {
+                if (m < p.m) {
+                    float v = acc[m];  // K order: rank 0 first, then 1, 2, ...
+                    for (int r = 1; r < p.split; ++r) v += red[((r - 1) * p.m + m) * kTileRows + row];
+                    p.y[static_cast<size_t>(m) * p.ldy + n_idx] = __float2bfloat16_rn(v * alpha);
+                }
+            }
+        }
+    }
+
+    // ---------------- teardown
+    tc_fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after_sync();
+        tmem_dealloc(tmem_d, kTmemCols);
+    }
+}
+
+// =====================================================================
+// CUDA-core M = 1 kernel
+// =====================================================================
+template <int CWARPS>
+__global__ void __launch_bounds__(32 * (CWARPS + 1), 1)
+    tinym_simt_m1_kernel(const __grid_constant__ CUtensorMap tm_w,
+                         const __grid_constant__ CUtensorMap tm_x, const TinymParams p) {
+    static_assert(CWARPS == 4 || CWARPS == 8, "CWARPS must be 4 or 8");
+    constexpr int kXStageBytes = kBlockK;  // one unswizzled 128-byte X row
+    constexpr uint32_t kStageTx = kWStageBytes + kXStageBytes;
+    constexpr int kRowsPerWarp = kTileRows / CWARPS;
+    constexpr int kPasses = kRowsPerWarp / 4;  // 4 rows per warp instruction
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = align1024(smem_raw);
+    const SmemLayout L = smem_layout(p.stages, kXStageBytes, p.split, 1);
+    const uint32_t s_base = smem_u32(smem);
+    const uint32_t w_ring = s_base + L.w_off;
+    const uint32_t x_ring = s_base + L.x_off;
+    const uint32_t bars = s_base + L.bar_off;
+    const int stages = p.stages;
+    auto full_bar = [&](int s) { return bars + 8u * s; };
+    auto empty_bar = [&](int s) { return bars + 8u * (stages + s); };
+    volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L.misc_off + 4);
+    float* red = reinterpret_cast<float*>(smem + L.red_off);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int split_idx = blockIdx.x;
+    const int tile = blockIdx.y;
+    const int kb0 = split_idx * p.kb_per_split;
+    const int kb1 = min(kb0 + p.kb_per_split, p.kb_total);
+    const int nkb = kb1 - kb0;
+
+    const WaitGuard guard{abort_flag, &g_err_word, p.timeout_ns};
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), CWARPS);
+        }
+        *abort_flag = 0u;
+        fence_mbar_init();
+        fence_proxy_async_smem();
+        tma_prefetch_desc(&tm_w);
+        tma_prefetch_desc(&tm_x);
+    }
+    __syncthreads();
+    if (p.split > 1) cluster_arrive_relaxed();
+
+    float acc[kPasses];
+#pragma unroll
+    for (int i = 0; i < kPasses; ++i) acc[i] = 0.f;
+    bool have_acc = false;
+    const int sub = lane >> 3;    // which of the 4 rows of a pass
+    const int chunk = lane & 7;   // which 16-byte chunk of the 128-byte row
+    const int rbase = (warp - 1) * kRowsPerWarp;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint64_t pol_w = l2_policy_evict_first();
+            const uint64_t pol_x = l2_policy_evict_last();
+            int issued = 0;
+            for (int i = 0; i < nkb; ++i) {
+                const int s = i % stages;
+                if (i >= stages) {
+                    if (!mbar_wait(empty_bar(s), ((i / stages) - 1) & 1, guard, kErrProducerWait))
+                        break;
+                }
+                const int kc = (kb0 + i) * kBlockK;
+                mbar_expect_tx(full_bar(s), kStageTx);
+                tma_load_2d(w_ring + s * kWStageBytes, &tm_w, full_bar(s), kc, tile * kTileRows,
+                            pol_w);
+                tma_load_2d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), kc, 0, pol_x);
+                ++issued;
+            }
+            if (*abort_flag) {
+                for (int j = max(0, issued - stages); j < issued; ++j)
+                    mbar_drain(full_bar(j % stages), (j / stages) & 1, guard, kErrDrain);
+            }
+        }
+    } else {
+        bool ok = true;
+        for (int i = 0; i < nkb; ++i) {
+            const int s = i % stages;
+            if (!mbar_wait(full_bar(s), (i / stages) & 1, guard, kErrConsumerWait)) {
+                ok = false;
+                break;
+            }
+            const uint8_t* xs = smem + L.x_off + s * kXStageBytes;
+            const uint8_t* ws = smem + L.w_off + s * kWStageBytes;
+            float xv[16];
+            {
+                const uint4 raw = *reinterpret_cast<const uint4*>(xs + chunk * 16);
+                const uint32_t wd[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 lo = e4m3x2_to_f32x2(wd[j]);
+                    const float2 hi = e4m3x2_to_f32x2(wd[j] >> 16);
+                    xv[4 * j + 0] = lo.x;
+                    xv[4 * j + 1] = lo.y;
+                    xv[4 * j + 2] = hi.x;
+                    xv[4 * j + 3] = hi.y;
+                }
+            }
+#pragma unroll
+            for (int pp = 0; pp < kPasses; ++pp) {
+                const int r = rbase + pp * 4 + sub;
+                const int phys = chunk ^ (r & 7);  // 128B swizzle: 16B chunk c of row r
+                const uint4 raw = *reinterpret_cast<const uint4*>(ws + r * kBlockK + phys * 16);
+                const uint32_t wd[4] = {raw.x, raw.y, raw.z, raw.w};
+                float a = acc[pp];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 lo = e4m3x2_to_f32x2(wd[j]);
+                    const float2 hi = e4m3x2_to_f32x2(wd[j] >> 16);
+                    a = fmaf(lo.x, xv[4 * j + 0], a);
+                    a = fmaf(lo.y, xv[4 * j + 1], a);
+                    a = fmaf(hi.x, xv[4 * j + 2], a);
+                    a = fmaf(hi.y, xv[4 * j + 3], a);
+                }
+                acc[pp] = a;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty_bar(s));
+        }
+        if (ok && !*abort_flag) {
+#pragma unroll
+            for (int pp = 0; pp < kPasses; ++pp) {
+                float v = acc[pp];
+                v += __shfl_xor_sync(0xFFFFFFFFu, v, 1);
+                v += __shfl_xor_sync(0xFFFFFFFFu, v, 2);
+                v += __shfl_xor_sync(0xFFFFFFFFu, v, 4);
+                acc[pp] = v;
+            }
+            have_acc = true;
+        }
+    }
+    __syncwarp();
+
+    const bool writer = have_acc && chunk == 0;
+    if (p.split == 1) {
+        if (writer) {
+            const float alpha = load_alpha(p);
+#pragma unroll
+            for (int pp = 0; pp < kPasses; ++pp) {
+                const int n_idx = tile * kTileRows + rbase + pp * 4 + sub;
+                if (n_idx < p.n) p.y[n_idx] = __float2bfloat16_rn(acc[pp] * alpha);
+            }
+        }
+    } else {
+        __syncwarp();
+        cluster_wait_acquire();
+        if (writer && split_idx > 0) {
+            const uint32_t remote = dsmem_map(smem_u32(red), 0);
+#pragma unroll
+            for (int pp = 0; pp < kPasses; ++pp)
+                dsmem_st_f32(remote + 4u * ((split_idx - 1) * kTileRows + rbase + pp * 4 + sub),
+                             acc[pp]);
+        }
+        __syncwarp();
+        cluster_arrive_release();
+        cluster_wait_acquire();
+        if (writer && split_idx == 0) {
+            const float alpha = load_alpha(p);
+#pragma unroll
+            for (int pp = 0; pp < kPasses; ++pp) {
+                const int r = rbase + pp * 4 + sub;
+                const int n_idx = tile * kTileRows + r;
+                if (n_idx < p.n) {
+                    float v = acc[pp];
+                    for (int q = 1; q < p.split; ++q) v += red[(q - 1) * kTileRows + r];
+                    p.y[n_idx] = __float2bfloat16_rn(v * alpha);
+                }
+            }
+        }
+    }
+    __syncthreads();
+}
+
+}  // namespace tinym

@@ -1,0 +1,214 @@
+"""B200-native tiny-M FP8 GEMM: Python side of the C ABI.
+
+Loads the in-tree native libraries and exposes
+
+* ``capi()``            -- the ctypes handle of ``libtinym_b200.so`` with the
+  signatures of ``include/tinym_b200.h``;
+* ``load_torch_op()``   -- registers ``torch.ops.sm120_fp8_gemm`` (the
+  reference's op namespace, src/torch_candidate_extension.cu:85-91);
+* ``gemm_ptr(...)``     -- one call through the C ABI on raw pointers (used by
+  the parity tests and the N-sharded wrapper);
+* ``select_plan(...)``  -- the shape-dispatch table (host only);
+* ``Plan``              -- ``tinym_plan`` as a ctypes structure.
+
+There is no CPU fallback: if the native library is missing or the GPU is
+not an sm_100 device, calls raise.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+from . import build as _build
+
+PKG = Path(__file__).resolve().parent
+CORE_SO = _build.CORE_SO
+TORCH_SO = _build.TORCH_SO
+
+TINYM_OK = 0
+STATUS_NAMES = {
+    0: "TINYM_OK",
+    1: "TINYM_ERR_INVALID_ARGUMENT",
+    2: "TINYM_ERR_UNSUPPORTED_SHAPE",
+    3: "TINYM_ERR_MISALIGNED",
+    4: "TINYM_ERR_CUDA",
+    5: "TINYM_ERR_UNSUPPORTED_DEVICE",
+    6: "TINYM_ERR_DEVICE_TIMEOUT",
+    7: "TINYM_ERR_BAD_PLAN",
+}
+KERNEL_TC = 1
+KERNEL_SIMT_M1 = 2
+
+# Every symbol include/tinym_b200.h declares (checked by the CPU tests).
+EXPORTED = (
+    "tinym_fp8_gemm",
+    "tinym_fp8_gemm_dev_alpha",
+    "tinym_fp8_gemm_ex",
+    "tinym_select_plan",
+    "tinym_check_plan",
+    "tinym_device_status",
+    "tinym_status_string",
+    "tinym_last_error",
+    "tinym_abi_version",
+)
+
+
+class Plan(ctypes.Structure):
+    """Mirror of ``tinym_plan`` (include/tinym_b200.h)."""
+
+    _fields_ = [
+        ("kernel", ctypes.c_int32),
+        ("split_k", ctypes.c_int32),
+        ("stages", ctypes.c_int32),
+        ("mma_n", ctypes.c_int32),
+        ("consumer_warps", ctypes.c_int32),
+        ("block_k", ctypes.c_int32),
+        ("tiles_n", ctypes.c_int32),
+        ("grid_ctas", ctypes.c_int32),
+        ("smem_bytes", ctypes.c_int32),
+        ("threads", ctypes.c_int32),
+    ]
+
+    def as_dict(self) -> dict:
+        return {name: int(getattr(self, name)) for name, _ in self._fields_}
+
+    def __repr__(self) -> str:  # pragma: no cover - debugging aid
+        return f"Plan({self.as_dict()})"
+
+
+class TinymError(RuntimeError):
+    """A non-zero tinym_status from the C ABI."""
+
+    def __init__(self, status: int, message: str):
+        self.status = status
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+
+
+_lock = threading.Lock()
+_capi = None
+_torch_op_loaded = False
+
+
+def capi() -> ctypes.CDLL:
+    """Load libtinym_b200.so (building it first if it is missing or stale)."""
+    global _capi
+    if _capi is not None:
+        return _capi
+    with _lock:
+        if _capi is None:
+            if not CORE_SO.exists():
+                _build.build_core()
+            lib = ctypes.CDLL(str(CORE_SO))
+            vp, i64, f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_float
+            lib.tinym_fp8_gemm.argtypes = [vp, vp, vp, i64, i64, i64, f32, f32, vp]
+            lib.tinym_fp8_gemm.restype = ctypes.c_int
+            lib.tinym_fp8_gemm_dev_alpha.argtypes = [vp, vp, vp, i64, i64, i64, vp, vp]
+            lib.tinym_fp8_gemm_dev_alpha.restype = ctypes.c_int
+            lib.tinym_fp8_gemm_ex.argtypes = [vp, vp, vp, i64, i64, i64, i64, vp, f32,
+                                              ctypes.POINTER(Plan), vp]
+            lib.tinym_fp8_gemm_ex.restype = ctypes.c_int
+            lib.tinym_select_plan.argtypes = [i64, i64, i64, ctypes.c_int32, ctypes.POINTER(Plan)]
+            lib.tinym_select_plan.restype = ctypes.c_int
+            lib.tinym_check_plan.argtypes = [i64, i64, i64, ctypes.POINTER(Plan)]
+            lib.tinym_check_plan.restype = ctypes.c_int
+            lib.tinym_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int32]
+            lib.tinym_device_status.restype = ctypes.c_int
+            lib.tinym_status_string.argtypes = [ctypes.c_int32]
+            lib.tinym_status_string.restype = ctypes.c_char_p
+            lib.tinym_last_error.argtypes = []
+            lib.tinym_last_error.restype = ctypes.c_char_p
+            lib.tinym_abi_version.argtypes = []
+            lib.tinym_abi_version.restype = ctypes.c_int32
+            _capi = lib
+    return _capi
+
+
+def _check(status: int) -> None:
+    if status != TINYM_OK:
+        msg = capi().tinym_last_error().decode(errors="replace")
+        raise TinymError(status, msg)
+
+
+def load_torch_op() -> None:
+    """Register torch.ops.sm120_fp8_gemm from the in-tree shim."""
+    global _torch_op_loaded
+    if _torch_op_loaded:
+        return
+    with _lock:
+        if not _torch_op_loaded:
+            import torch
+
+            if not TORCH_SO.exists():
+                _build.build_torch_op()
+            torch.ops.load_library(str(TORCH_SO))
+            _torch_op_loaded = True
+
+
+def select_plan(m: int, n: int, k: int, sm_count: int = 148) -> Plan:
+    """The shape-dispatch table's choice for (m, n, k) on sm_count SMs."""
+    p = Plan()
+    _check(capi().tinym_select_plan(m, n, k, sm_count, ctypes.byref(p)))
+    return p
+
+
+def check_plan(m: int, n: int, k: int, plan: Plan) -> Plan:
+    """Validate an explicit plan and fill its derived fields."""
+    p = Plan.from_buffer_copy(plan)
+    _check(capi().tinym_check_plan(m, n, k, ctypes.byref(p)))
+    return p
+
+
+def make_plan(kernel: int = KERNEL_TC, split_k: int = 1, stages: int = 4, mma_n: int = 16,
+              consumer_warps: int = 0) -> Plan:
+    p = Plan()
+    p.kernel, p.split_k, p.stages, p.mma_n = kernel, split_k, stages, mma_n
+    p.consumer_warps, p.block_k = consumer_warps, 128
+    return p
+
+
+def gemm_ptr(x_ptr: int, w_ptr: int, y_ptr: int, m: int, n: int, k: int, *,
+             ldy: int | None = None, alpha: float = 1.0, alpha_ptr: int | None = None,
+             plan: Plan | None = None, stream: int = 0) -> None:
+    """Y = alpha * X . W^T through tinym_fp8_gemm_ex on raw device pointers."""
+    lib = capi()
+    pl = ctypes.byref(plan) if plan is not None else None
+    st = lib.tinym_fp8_gemm_ex(x_ptr, w_ptr, y_ptr, n if ldy is None else ldy, m, n, k,
+                               alpha_ptr, alpha, pl, stream)
+    _check(st)
+
+
+def device_status(clear: bool = True) -> int:
+    """Device error word (bounded-wait timeouts); synchronises the device."""
+    flags = ctypes.c_uint32(0)
+    st = capi().tinym_device_status(ctypes.byref(flags), 1 if clear else 0)
+    if st not in (TINYM_OK, 6):
+        _check(st)
+    return int(flags.value)
+
+
+def gemm(x, w, alpha, *, out=None, plan: Plan | None = None):
+    """torch convenience wrapper over the C ABI (device alpha, current stream)."""
+    import torch
+
+    if x.dtype != torch.float8_e4m3fn or w.dtype != torch.float8_e4m3fn:
+        raise ValueError("x and w must be float8_e4m3fn")
+    m, k = x.shape
+    n = w.shape[0]
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    stream = torch.cuda.current_stream(x.device).cuda_stream
+    if isinstance(alpha, torch.Tensor):
+        gemm_ptr(x.data_ptr(), w.data_ptr(), out.data_ptr(), m, n, k, ldy=out.stride(0),
+                 alpha_ptr=alpha.data_ptr(), plan=plan, stream=stream)
+    else:
+        gemm_ptr(x.data_ptr(), w.data_ptr(), out.data_ptr(), m, n, k, ldy=out.stride(0),
+                 alpha=float(alpha), plan=plan, stream=stream)
+    return out
+
+
+__all__ = [
+    "capi", "load_torch_op", "select_plan", "check_plan", "make_plan", "gemm_ptr", "gemm",
+    "device_status", "Plan", "TinymError", "EXPORTED", "KERNEL_TC", "KERNEL_SIMT_M1",
+]

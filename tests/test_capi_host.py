@@ -1,0 +1,162 @@
+"""CPU: the C-ABI library loads, exports every declared symbol, and its
+host-side logic (shape gate, dispatch table, plan validation, argument
+checks) behaves as documented.  No kernel is launched here."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "tinym_b200.h"
+
+OFFICIAL = [(1, 5120, 16384), (9, 5120, 16384), (1, 6144, 5120), (9, 6144, 5120),
+            (1, 5120, 8192), (9, 5120, 8192)]
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"TINYM_API\s+[\w\s\*]+?\b(tinym_\w+)\s*\(", text)))
+
+
+def test_header_and_binding_agree():
+    import tinym_b200
+
+    assert declared_symbols() == sorted(tinym_b200.EXPORTED)
+
+
+def test_library_exports_every_declared_symbol():
+    import tinym_b200
+
+    lib = tinym_b200.capi()
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    assert lib.tinym_abi_version() == 1
+
+
+def test_status_strings():
+    import tinym_b200
+
+    lib = tinym_b200.capi()
+    for code, name in tinym_b200.STATUS_NAMES.items():
+        assert lib.tinym_status_string(code).decode() == name
+    assert lib.tinym_status_string(99).decode() == "TINYM_ERR_UNKNOWN"
+
+
+def test_plan_struct_layout():
+    import tinym_b200
+
+    assert ctypes.sizeof(tinym_b200.Plan) == 40
+
+
+@pytest.mark.parametrize("m,k,n", OFFICIAL)
+def test_dispatch_table_official_points(m, k, n):
+    """Every official point gets a plan that fits 227 KiB of shared memory and
+    one wave on 148 SMs."""
+    import tinym_b200
+
+    p = tinym_b200.select_plan(m, n, k, 148)
+    assert p.grid_ctas <= 148
+    assert p.smem_bytes <= 232448
+    assert p.tiles_n == (n + 127) // 128
+    kb = (k + 127) // 128
+    per = -(-kb // p.split_k)
+    assert (p.split_k - 1) * per < kb  # no empty K range
+    if p.kernel == tinym_b200.KERNEL_TC:
+        assert p.mma_n >= m and p.mma_n in (8, 16)
+    else:
+        assert m == 1
+
+
+def test_dispatch_fills_small_sm_counts():
+    import tinym_b200
+
+    p = tinym_b200.select_plan(9, 5120, 6144, 40)
+    assert p.grid_ctas <= 40 or p.split_k == 1
+    p = tinym_b200.select_plan(1, 128, 128, 148)
+    assert p.split_k == 1  # one K block cannot be split
+
+
+@pytest.mark.parametrize("m", list(range(1, 17)))
+def test_dispatch_every_m(m):
+    import tinym_b200
+
+    for k, n in ((6144, 5120), (5120, 8192), (5120, 16384), (16, 1), (4096, 100000)):
+        p = tinym_b200.select_plan(m, n, k, 148)
+        assert p.grid_ctas >= 1 and p.stages >= 2
+
+
+def test_shape_gate():
+    import tinym_b200
+
+    for m, n, k, status in [(17, 128, 128, 2), (0, 128, 128, 1), (1, 0, 128, 1),
+                            (1, 128, 40, 2), (1, 128, 0, 1)]:
+        with pytest.raises(tinym_b200.TinymError) as ei:
+            tinym_b200.select_plan(m, n, k, 148)
+        assert ei.value.status == status
+
+
+def test_check_plan_rejects_bad_plans():
+    import tinym_b200 as t
+
+    good = t.check_plan(1, 1024, 1024, t.make_plan(t.KERNEL_SIMT_M1, 2, 4, 0, 8))
+    assert good.threads == 288 and good.grid_ctas == 16
+    bad = [
+        (2, t.make_plan(t.KERNEL_SIMT_M1, 1, 4, 0, 4)),    # SIMT needs M == 1
+        (9, t.make_plan(t.KERNEL_TC, 1, 4, 8)),             # MMA N < M
+        (1, t.make_plan(t.KERNEL_TC, 9, 4, 8)),             # cluster > 8
+        (1, t.make_plan(t.KERNEL_TC, 1, 1, 8)),             # ring too shallow
+        (1, t.make_plan(t.KERNEL_TC, 1, 4, 12)),            # MMA N not 8/16
+        (1, t.make_plan(7, 1, 4, 8)),                       # unknown kernel
+        (1, t.make_plan(t.KERNEL_TC, 8, 4, 8)),             # 8 splits of 7 K blocks
+    ]
+    for m, plan in bad:
+        with pytest.raises(t.TinymError) as ei:
+            t.check_plan(m, 1024, 896, plan)
+        assert ei.value.status == 7, (m, plan.as_dict())
+
+
+def test_argument_checks_before_any_cuda_call():
+    """Null / misaligned pointers and bad ldy are rejected on the host."""
+    import tinym_b200 as t
+
+    lib = t.capi()
+    st = lib.tinym_fp8_gemm_ex(None, 16, 16, 128, 1, 128, 128, None, 1.0, None, None)
+    assert st == 1
+    st = lib.tinym_fp8_gemm_ex(17, 32, 64, 128, 1, 128, 128, None, 1.0, None, None)
+    assert st == 3 and b"16-byte" in lib.tinym_last_error()
+    st = lib.tinym_fp8_gemm_ex(16, 32, 65, 128, 1, 128, 128, None, 1.0, None, None)
+    assert st == 3
+    st = lib.tinym_fp8_gemm_ex(16, 32, 64, 64, 1, 128, 128, None, 1.0, None, None)
+    assert st == 1 and b"ldy" in lib.tinym_last_error()
+    st = lib.tinym_fp8_gemm_ex(16, 32, 64, 128, 1, 128, 128, None, float("inf"), None, None)
+    assert st == 1
+    st = lib.tinym_fp8_gemm_dev_alpha(16, 32, 64, 1, 128, 128, None, None)
+    assert st == 1
+    st = lib.tinym_fp8_gemm(16, 32, 64, 20, 128, 128, 1.0, 1.0, None)
+    assert st == 2
+
+
+def test_torch_op_registers_reference_schema():
+    import torch
+
+    import tinym_b200
+
+    tinym_b200.load_torch_op()
+    schema = str(torch.ops.sm120_fp8_gemm.run.default._schema)
+    assert schema == "sm120_fp8_gemm::run(Tensor a, Tensor b, float alpha) -> Tensor"
+    assert "run_alpha_tensor" in str(torch.ops.sm120_fp8_gemm.run_alpha_tensor.default._schema)
+
+
+def test_candidate_kernel_surface():
+    """Same public names and validation as the reference adapter."""
+    import torch
+
+    import candidate_kernel
+
+    assert candidate_kernel.__all__ == ["build", "prepare_weights", "fp8_gemm"]
+    with pytest.raises(ValueError):
+        candidate_kernel.prepare_weights(torch.zeros(4, 4))
+    assert candidate_kernel.build() is True

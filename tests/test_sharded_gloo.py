@@ -1,0 +1,91 @@
+"""CPU: the N-sharded wrapper's host logic on world_size-2 gloo ranks.
+
+The local GEMM is replaced by the CPU oracle (test infrastructure), so this
+checks sharding, padding and the all-gather reassembly, not the kernel."""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+@pytest.mark.parametrize("n,world", [(5120, 2), (16384, 8), (300, 2), (100, 4), (3, 2),
+                                     (129, 3), (1, 2)])
+def test_shard_bounds_cover_exactly(n, world):
+    from tinym_b200.sharded import shard_bounds
+
+    bounds = [shard_bounds(n, world, r) for r in range(world)]
+    assert bounds[0][0] == 0 and bounds[-1][1] == n
+    for (a0, b0), (a1, b1) in zip(bounds, bounds[1:]):
+        assert b0 == a1 and a0 <= b0
+    if -(-n // 128) >= world:
+        assert all(a % 128 == 0 for a, _ in bounds)
+        sizes = [b - a for a, b in bounds]
+        assert max(sizes) - min(sizes) <= 128
+
+
+def _worker(rank, world, port, m, k, n, q):
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        import sys
+        from pathlib import Path
+
+        root = Path(__file__).resolve().parents[1]
+        sys.path.insert(0, str(root))
+        sys.path.insert(0, str(root / "sm120-fp8-gemm-submit_b200"))
+        from oracle import fp8_oracle as orc
+        from tinym_b200.sharded import ShardedFp8Gemm
+
+        xq, wq, sx, sw, alpha = orc.make_case(m, k, n, seed=42, dist="normal")
+
+        def cpu_gemm(x, w_local, a, out):
+            ref = orc.reference(x.numpy(), w_local.numpy(), a.numpy())
+            out.copy_(torch.from_numpy(ref).to(torch.bfloat16))
+            return out
+
+        g = ShardedFp8Gemm.from_full_weight(torch.from_numpy(wq), local_gemm=cpu_gemm)
+        y = g(torch.from_numpy(xq), torch.from_numpy(alpha))
+        full = orc.reference(xq, wq, alpha)
+        rel = orc.max_rel_err(y.float().numpy(), full)
+        q.put((rank, tuple(y.shape), rel, g.start, g.stop))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # pragma: no cover - reported to the parent
+        q.put((rank, "error", repr(e), 0, 0))
+
+
+@pytest.mark.parametrize("m,k,n", [(9, 256, 640), (1, 128, 300), (16, 128, 5)])
+def test_sharded_gather_gloo_world2(m, k, n):
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, m, k, n, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, shape, rel, a, b in res:
+        assert shape == (m, n), (rank, shape, rel)
+        assert rel <= 4e-3
+    spans = sorted((a, b) for _, _, _, a, b in res)
+    assert spans[0][0] == 0 and spans[-1][1] == n and spans[0][1] == spans[1][0]

@@ -167,23 +167,72 @@ def make_operands(m, k, n, n_sets, device, seed=0):
     return sets
 
 
-def time_launches(fn, sets, steps, warmup, stream):
-    """Per-launch CUDA-event durations (ms) plus the total span (ms)."""
+SPACER_CYCLES = 100_000  # ~50 us of GPU spin ahead of each latency sample
+
+
+def per_launch_latency(fn, sets, n, flush=None):
+    """Cold-L2 latency of single launches (ms each), measured on the device.
+
+    Each sample is  [spacer] -> start event -> fn(set) -> end event.  The
+    spacer keeps the GPU busy while the host enqueues the sample, so host
+    launch overhead never shows up as device time.  flush=None: the spacer
+    is a spin kernel and the rotation over `sets` keeps W cold; flush=<buf>:
+    the reference harness's protocol (zero a 256 MiB buffer before each
+    launch, fp8_gemm_task_harness.py:84-96), which also leaves L2 full of
+    dirty lines that the timed launch must write back.
+    """
     import torch
 
-    for i in range(warmup):
-        fn(sets[i % len(sets)])
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+    stream = torch.cuda.current_stream()
     torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        for i in range(steps):
-            starts[i].record(stream)
-            fn(sets[i % len(sets)])
-            ends[i].record(stream)
+    for i in range(n):
+        if flush is None:
+            torch.cuda._sleep(SPACER_CYCLES)
+        else:
+            flush.zero_()
+        starts[i].record(stream)
+        fn(sets[i % len(sets)], stream.cuda_stream)
+        ends[i].record(stream)
     torch.cuda.synchronize()
-    per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    return per, starts[0].elapsed_time(ends[-1])
+    return [s.elapsed_time(e) for s, e in zip(starts, ends)]
+
+
+def graph_throughput(fn, sets, steps, warmup):
+    """Time exactly `steps` back-to-back launches (rotating over `sets`)
+    replayed from CUDA graphs; returns total device ms.  Graph replay keeps
+    the GPU fed, so this is the kernel's sustained rate, not the host's."""
+    import torch
+
+    chunk = min(steps, 4 * len(sets))
+    graphs = []
+    for size in sorted({chunk, steps % chunk} - {0}, reverse=True):
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for i in range(3):  # warm-up on the capture stream
+                fn(sets[i % len(sets)], s.cuda_stream)
+        torch.cuda.current_stream().wait_stream(s)
+        with torch.cuda.graph(g):
+            cs = torch.cuda.current_stream().cuda_stream
+            for i in range(size):
+                fn(sets[i % len(sets)], cs)
+        graphs.append((size, g))
+    full = {size: g for size, g in graphs}
+    for _ in range(max(1, warmup // chunk)):
+        full[chunk].replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps // chunk):
+        full[chunk].replay()
+    if steps % chunk:
+        full[steps % chunk].replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1)
 
 
 def cpu_baseline(m, k, n, budget_s=10.0):
@@ -239,7 +288,7 @@ def run_reference_arm(args, m, k, n):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--steps", type=int, default=200000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
@@ -287,19 +336,24 @@ def main():
     sm_count = torch.cuda.get_device_properties(device).multi_processor_count
     plan = tinym_b200.select_plan(m, n_local, k, sm_count)
 
-    def ours(s):
+    def ours(s, stream_handle):
         x, w, y, sx, sw, alpha = s
         tinym_b200.gemm_ptr(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n_local, k,
-                            alpha_ptr=alpha.data_ptr(), stream=stream.cuda_stream)
+                            alpha_ptr=alpha.data_ptr(), stream=stream_handle)
 
-    # ---- timed region: K steps, barrier + synchronize on both sides
+    # ---- cold-L2 per-launch latency (spacer protocol), untimed for `value`
     for i in range(args.warmup):
-        ours(sets[i % n_sets])
+        ours(sets[i % n_sets], stream.cuda_stream)
+    lat_n = max(50, min(args.steps, 2000))
+    per = per_launch_latency(ours, sets, lat_n)
+    median_us = statistics.median(per) * 1e3
+
+    # ---- timed region: exactly K steps, barrier + synchronize on both sides
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local_rank) as clk:
-        per, span = time_launches(ours, sets, args.steps, 0, stream)
+        span = graph_throughput(ours, sets, args.steps, args.warmup)
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
@@ -313,8 +367,7 @@ def main():
     span_max = float(span_t.item())
     total_bytes = algo_bytes(m, k, n_local) * world * args.steps
     value_gbs = total_bytes / (span_max * 1e-3) / 1e9
-    median_us = statistics.median(per) * 1e3
-    mean_us = statistics.fmean(per) * 1e3
+    mean_us = span_max / args.steps * 1e3  # average launch duration in the timed region
 
     # optional all-gather of Y (timed separately)
     allgather_us = None
@@ -355,9 +408,12 @@ def main():
                                   f"({n_sets * set_bytes / 2**20:.0f} MiB > 2x L2 "
                                   f"{l2 / 2**20:.0f} MiB)",
                        "plan": plan.as_dict()},
-            "median_us": round(median_us, 3), "mean_us": round(mean_us, 3),
+            "median_us": round(median_us, 3),
             "p10_us": round(sorted(per)[len(per) // 10] * 1e3, 3),
             "p90_us": round(sorted(per)[(9 * len(per)) // 10] * 1e3, 3),
+            "latency_protocol": f"{lat_n} single launches, each after a GPU spin spacer, "
+                                "rotating buffers (cold W), CUDA events",
+            "graph_us_per_launch": round(mean_us, 3),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_source": f"{peak_note} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
@@ -371,17 +427,28 @@ def main():
 
     # ---- cuBLASLt competitor (1 GPU only, same buffers / protocol)
     if rank == 0 and world == 1 and not args.no_cublas:
-        def cublas(s):
+        def cublas(s, stream_handle):
             x, w, y, sx, sw, alpha = s
             torch._scaled_mm(x, w.t(), scale_a=sx, scale_b=sw, out_dtype=torch.bfloat16)
 
-        cb_steps = min(args.steps, 5000)
-        per_cb, _ = time_launches(cublas, sets, cb_steps, args.warmup, stream)
+        for i in range(args.warmup):
+            cublas(sets[i % n_sets], stream.cuda_stream)
+        per_cb = per_launch_latency(cublas, sets, lat_n)
         out["cublas_median_us"] = round(statistics.median(per_cb) * 1e3, 3)
         out["speedup_vs_cublas"] = round(out["cublas_median_us"] / median_us, 4)
+        cb_span = graph_throughput(cublas, sets, min(args.steps, 4000), args.warmup)
+        out["cublas_graph_us_per_launch"] = round(cb_span / min(args.steps, 4000) * 1e3, 3)
+        # the reference harness's own protocol (256 MiB memset before each launch)
+        flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=device)
+        h_n = min(lat_n, 300)
+        out["harness_protocol_median_us"] = {
+            "ours": round(statistics.median(per_launch_latency(ours, sets, h_n, flush)) * 1e3, 3),
+            "cublas": round(statistics.median(per_launch_latency(cublas, sets, h_n, flush)) * 1e3,
+                            3)}
+        del flush
 
     # ---- end to end through the public API with host buffers (1 GPU)
-    if world == 1:
+    if world == 1 and args.e2e_steps > 0:
         x, w, y, sx, sw, alpha = sets[0]
         hx = x.view(torch.uint8).cpu().pin_memory()
         hw = w.view(torch.uint8).cpu().pin_memory()

@@ -42,6 +42,11 @@ constexpr int kMaxStages = 12;
 constexpr int kSmemLimit = 232448; // 227 KiB opt-in per CTA on sm_100
 constexpr uint64_t kDefaultTimeoutNs = 1000000000ull;  // 1 s per wait
 
+// Build-time tuning knob: L2 sector promotion of the TMA tensor maps.
+#ifndef TINYM_L2_PROMOTION
+#define TINYM_L2_PROMOTION CU_TENSOR_MAP_L2_PROMOTION_L2_256B
+#endif
+
 thread_local char t_last_error[512] = "";
 
 int fail(int status, const char* fmt, ...) {
@@ -156,7 +161,7 @@ int get_map(const void* ptr, int64_t rows, int64_t cols, int box_rows, int swizz
     CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                        TINYM_L2_PROMOTION, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
         return fail(TINYM_ERR_CUDA,
                     "cuTensorMapEncodeTiled failed (CUresult %d) for [%lld x %lld] box %d rows",

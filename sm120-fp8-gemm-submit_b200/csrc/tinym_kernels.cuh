@@ -133,7 +133,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     const WaitGuard guard{abort_flag, &g_err_word, p.timeout_ns};
 
+    // The producer thread initialises the barriers and immediately puts the
+    // first ring-full of loads in flight, so the DRAM latency of the first
+    // bytes overlaps the TMEM allocation and the CTA-wide sync below.
+    int issued = 0;
+    uint64_t pol_w = 0, pol_x = 0;
+    auto issue = [&](int i) {
+        const int s = i % stages;
+        const int kc = (kb0 + i) * kBlockK;
+        mbar_expect_tx(full_bar(s), kStageTx);
+        tma_load_2d(w_ring + s * kWStageBytes, &tm_w, full_bar(s), kc, tile * kTileRows, pol_w);
+        tma_load_2d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), kc, 0, pol_x);
+    };
     if (threadIdx.x == 0) {
+        tma_prefetch_desc(&tm_w);
+        tma_prefetch_desc(&tm_x);
         for (int s = 0; s < stages; ++s) {
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), 1);
@@ -142,10 +156,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         *abort_flag = 0u;
         fence_mbar_init();
         fence_proxy_async_smem();
-    }
-    if (warp == 0 && lane == 0) {
-        tma_prefetch_desc(&tm_w);
-        tma_prefetch_desc(&tm_x);
+        pol_w = l2_policy_w();
+        pol_x = l2_policy_evict_last();
+        for (; issued < min(stages, nkb); ++issued) issue(issued);
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(tmem_slot), kTmemCols);
@@ -164,22 +177,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            // ---------------- TMA producer
-            const uint64_t pol_w = l2_policy_evict_first();
-            const uint64_t pol_x = l2_policy_evict_last();
-            int issued = 0;
-            for (int i = 0; i < nkb; ++i) {
-                const int s = i % stages;
-                if (i >= stages) {
-                    if (!mbar_wait(empty_bar(s), ((i / stages) - 1) & 1, guard, kErrProducerWait))
-                        break;
-                }
-                const int kc = (kb0 + i) * kBlockK;
-                mbar_expect_tx(full_bar(s), kStageTx);
-                tma_load_2d(w_ring + s * kWStageBytes, &tm_w, full_bar(s), kc, tile * kTileRows,
-                            pol_w);
-                tma_load_2d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), kc, 0, pol_x);
-                ++issued;
+            // ---------------- TMA producer (refills the ring as slots free up)
+            for (; issued < nkb; ++issued) {
+                const int s = issued % stages;
+                if (!mbar_wait(empty_bar(s), ((issued / stages) - 1) & 1, guard, kErrProducerWait))
+                    break;
+                issue(issued);
             }
             if (*abort_flag) {
                 // Drain the copies still in flight before shared memory is released.
@@ -306,7 +309,18 @@ __global__ void __launch_bounds__(32 * (CWARPS + 1), 1)
 
     const WaitGuard guard{abort_flag, &g_err_word, p.timeout_ns};
 
+    int issued = 0;
+    uint64_t pol_w = 0, pol_x = 0;
+    auto issue = [&](int i) {
+        const int s = i % stages;
+        const int kc = (kb0 + i) * kBlockK;
+        mbar_expect_tx(full_bar(s), kStageTx);
+        tma_load_2d(w_ring + s * kWStageBytes, &tm_w, full_bar(s), kc, tile * kTileRows, pol_w);
+        tma_load_2d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), kc, 0, pol_x);
+    };
     if (threadIdx.x == 0) {
+        tma_prefetch_desc(&tm_w);
+        tma_prefetch_desc(&tm_x);
         for (int s = 0; s < stages; ++s) {
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), CWARPS);
@@ -314,8 +328,9 @@ __global__ void __launch_bounds__(32 * (CWARPS + 1), 1)
         *abort_flag = 0u;
         fence_mbar_init();
         fence_proxy_async_smem();
-        tma_prefetch_desc(&tm_w);
-        tma_prefetch_desc(&tm_x);
+        pol_w = l2_policy_w();
+        pol_x = l2_policy_evict_last();
+        for (; issued < min(stages, nkb); ++issued) issue(issued);  // first ring-full
     }
     __syncthreads();
     if (p.split > 1) cluster_arrive_relaxed();
@@ -330,21 +345,11 @@ __global__ void __launch_bounds__(32 * (CWARPS + 1), 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            const uint64_t pol_w = l2_policy_evict_first();
-            const uint64_t pol_x = l2_policy_evict_last();
-            int issued = 0;
-            for (int i = 0; i < nkb; ++i) {
-                const int s = i % stages;
-                if (i >= stages) {
-                    if (!mbar_wait(empty_bar(s), ((i / stages) - 1) & 1, guard, kErrProducerWait))
-                        break;
-                }
-                const int kc = (kb0 + i) * kBlockK;
-                mbar_expect_tx(full_bar(s), kStageTx);
-                tma_load_2d(w_ring + s * kWStageBytes, &tm_w, full_bar(s), kc, tile * kTileRows,
-                            pol_w);
-                tma_load_2d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), kc, 0, pol_x);
-                ++issued;
+            for (; issued < nkb; ++issued) {
+                const int s = issued % stages;
+                if (!mbar_wait(empty_bar(s), ((issued / stages) - 1) & 1, guard, kErrProducerWait))
+                    break;
+                issue(issued);
             }
             if (*abort_flag) {
                 for (int j = max(0, issued - stages); j < issued; ++j)

@@ -142,6 +142,20 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
     asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
     return p;
 }
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// Build-time tuning knob: L2 priority of the streamed W tiles
+// (1 = evict_first, the default; 0 = evict_normal).
+#ifndef TINYM_W_EVICT_FIRST
+#define TINYM_W_EVICT_FIRST 1
+#endif
+__device__ __forceinline__ uint64_t l2_policy_w() {
+    return TINYM_W_EVICT_FIRST ? l2_policy_evict_first() : l2_policy_evict_normal();
+}
 
 // ---------------------------------------------------------------- tcgen05
 // Tensor-memory allocation (whole warp, .sync.aligned).  The allocated base

@@ -67,7 +67,7 @@ typedef enum tinym_status {
 /* A launch plan: which kernel and how the problem is cut.  Produced by
  * tinym_select_plan (the shape-dispatch table, replacing the hard-coded
  * six-way template dispatch of src/torch_candidate_extension.cu:60-78) and
- * accepted back by tinym_fp8_gemm_plan for sweeps. */
+ * accepted back by tinym_fp8_gemm_ex for sweeps. */
 typedef struct tinym_plan {
     int32_t kernel;         /* TINYM_KERNEL_* */
     int32_t split_k;        /* CTAs per 128-row W tile (K split, 1..8); >1 => cluster of split_k CTAs */
@@ -115,11 +115,33 @@ TINYM_API int tinym_select_plan(int64_t m, int64_t n, int64_t k, int32_t sm_coun
 /* Validate a plan for (m, n, k) and fill its derived fields.  Host-only. */
 TINYM_API int tinym_check_plan(int64_t m, int64_t n, int64_t k, tinym_plan* plan);
 
+/* How many clusters of `plan` (for this M, N, K) the current device can
+ * hold resident at once (CTAs for split_k == 1), from the CUDA occupancy
+ * calculator.  A grid of tiles_n clusters runs in one wave when this is
+ * >= tiles_n; the automatic dispatch shrinks split_k until it is.  No
+ * reference counterpart (the reference launches at most one CTA per SM,
+ * include/fp8_gemm_tinym.cuh:757-766). */
+TINYM_API int tinym_plan_max_active_clusters(int64_t m, int64_t n, int64_t k,
+                                             const tinym_plan* plan, int32_t* out);
+
 /* Device error word of the current device: bit flags set by kernels whose
  * bounded waits expired (0 = none).  Synchronises the device.  clear != 0
  * resets the word.  The reference has no counterpart (its waits spin
  * forever, include/fp8_gemm_tinym.cuh:164-176). */
 TINYM_API int tinym_device_status(uint32_t* flags, int32_t clear);
+
+/* Failure-detection self-test: launches the GEMM (plan = NULL for the
+ * dispatch table's choice) with fault injection that makes the producer
+ * issue no copies, so every consumer wait runs out after timeout_ns
+ * (1 .. 1e10 ns).  The kernel then sets bits in the device error word,
+ * releases its tensor memory and exits; no GPU fault occurs and the context
+ * stays usable.  Read the bits with tinym_device_status.  Y is left
+ * unspecified.  No reference counterpart (the reference's waits are
+ * unbounded). */
+TINYM_API int tinym_selftest_wait_timeout(const void* x, const void* w, void* y,
+                                          int64_t m, int64_t n, int64_t k,
+                                          const tinym_plan* plan, uint64_t timeout_ns,
+                                          void* stream);
 
 /* Human-readable name of a tinym_status code (static string). */
 TINYM_API const char* tinym_status_string(int32_t status);

@@ -40,6 +40,9 @@ constexpr int kMaxDevices = 64;
 constexpr int kMaxSplit = 8;       // portable cluster size
 constexpr int kMaxStages = 12;
 constexpr int kSmemLimit = 232448; // 227 KiB opt-in per CTA on sm_100
+// Per-CTA budget for two resident CTAs per SM: 228 KiB per SM, less 1 KiB
+// reserved per CTA, halved.
+constexpr uint32_t kSmemTwoPerSm = (233472u - 2u * 1024u) / 2u;
 constexpr uint64_t kDefaultTimeoutNs = 1000000000ull;  // 1 s per wait
 
 // Build-time tuning knob: L2 sector promotion of the TMA tensor maps.
@@ -180,6 +183,14 @@ int x_stage_bytes(const tinym_plan& p) {
     return p.kernel == TINYM_KERNEL_TC ? p.mma_n * kBlockK : kBlockK;
 }
 
+// Dynamic shared memory of a plan.  The TC kernel receives split-K partials
+// in its W ring (no separate buffer); the SIMT kernel keeps a separate
+// (split - 1) x 128-float buffer.
+uint32_t plan_smem_bytes(const tinym_plan& p) {
+    if (p.kernel == TINYM_KERNEL_TC) return tinym::smem_layout(p.stages, x_stage_bytes(p), 1, 0).bytes;
+    return tinym::smem_layout(p.stages, x_stage_bytes(p), p.split_k, kTileRows * 4).bytes;
+}
+
 int fill_derived(int64_t m, int64_t n, int64_t k, tinym_plan* p) {
     const int64_t tiles = (n + kTileRows - 1) / kTileRows;
     const int64_t kb = (k + kBlockK - 1) / kBlockK;
@@ -208,14 +219,18 @@ int fill_derived(int64_t m, int64_t n, int64_t k, tinym_plan* p) {
     if (p->stages < 2 || p->stages > kMaxStages)
         return fail(TINYM_ERR_BAD_PLAN, "plan.stages must be in 2..%d", kMaxStages);
     if (tiles > 65535) return fail(TINYM_ERR_UNSUPPORTED_SHAPE, "N too large (%lld tiles)", (long long)tiles);
-    const tinym::SmemLayout L = tinym::smem_layout(p->stages, x_stage_bytes(*p), p->split_k,
-                                                   static_cast<int>(m));
-    if (L.bytes > static_cast<uint32_t>(kSmemLimit))
-        return fail(TINYM_ERR_BAD_PLAN, "plan needs %u bytes of shared memory (> %d)", L.bytes,
+    const uint32_t smem = plan_smem_bytes(*p);
+    if (smem > static_cast<uint32_t>(kSmemLimit))
+        return fail(TINYM_ERR_BAD_PLAN, "plan needs %u bytes of shared memory (> %d)", smem,
                     kSmemLimit);
+    if (p->kernel == TINYM_KERNEL_TC &&
+        (p->split_k - 1) * tinym::tc_red_rank_bytes(p->mma_n) > p->stages * tinym::kWStageBytes)
+        return fail(TINYM_ERR_BAD_PLAN,
+                    "split_k %d needs %d bytes of partial sums, more than the %d-stage ring holds",
+                    p->split_k, (p->split_k - 1) * tinym::tc_red_rank_bytes(p->mma_n), p->stages);
     p->tiles_n = static_cast<int32_t>(tiles);
     p->grid_ctas = static_cast<int32_t>(tiles * p->split_k);
-    p->smem_bytes = static_cast<int32_t>(L.bytes);
+    p->smem_bytes = static_cast<int32_t>(smem);
     return TINYM_OK;
 }
 
@@ -235,31 +250,149 @@ int check_shape(int64_t m, int64_t n, int64_t k) {
     return TINYM_OK;
 }
 
-// Heuristic part of the dispatch table: the largest K split (cluster size)
-// that keeps every (tile, split) CTA in one wave of sm_count CTAs, leaves
-// every CTA at least 2 K blocks, and stays within the portable cluster size.
-int heuristic_split(int64_t tiles, int64_t kb, int sm_count) {
-    int best = 1;
-    for (int s = 2; s <= kMaxSplit; ++s) {
-        if (tiles * s > sm_count) break;
-        const int64_t per = (kb + s - 1) / s;
-        if (per < 2 || (s - 1) * per >= kb) continue;
-        best = s;
-    }
-    return best;
+// Ring depth for a TC plan: enough stages to cover the CTA's K blocks (no
+// more is useful) and to hold the split-K partials the leader receives in
+// its ring, at most max_st; -1 if the partials cannot fit.
+int tc_stages_for(int split, int64_t kb_per_cta, int mma_n, int max_st) {
+    const int red = (split - 1) * tinym::tc_red_rank_bytes(mma_n);
+    const int need_red = (red + tinym::kWStageBytes - 1) / tinym::kWStageBytes;
+    const int64_t st = std::max<int64_t>({2, kb_per_cta < max_st ? kb_per_cta : max_st, need_red});
+    return st > max_st ? -1 : static_cast<int>(st);
 }
 
-int max_stages_fitting(const tinym_plan& p, int64_t m) {
+// Largest ring depth whose shared memory fits `limit` bytes.
+int max_stages_fitting(const tinym_plan& p, uint32_t limit) {
     int st = kMaxStages;
     while (st > 2) {
         tinym_plan q = p;
         q.stages = st;
-        if (tinym::smem_layout(st, x_stage_bytes(q), q.split_k, static_cast<int>(m)).bytes <=
-            static_cast<uint32_t>(kSmemLimit))
-            break;
+        if (plan_smem_bytes(q) <= limit) break;
         --st;
     }
     return st;
+}
+
+// Heuristic part of the dispatch table.  Tiled TMA streams saturate HBM
+// only with every SM busy, and a CTA alone cannot pull an SM's share, so
+// the search covers one and two CTAs per SM: for each, the largest K split
+// (cluster size <= 8) that keeps tiles * split CTAs within one wave, leaves
+// each CTA >= 2 K blocks and fits its partial sums in the ring.  The option
+// filling more of the GPU's CTA slots wins (ties: two CTAs per SM).
+tinym_plan heuristic_plan(int64_t m, int64_t tiles, int64_t kb, int sm_count) {
+    tinym_plan best{};
+    double best_fill = -1.0;
+    for (int per_sm = 2; per_sm >= 1; --per_sm) {
+        const uint32_t limit = per_sm == 2 ? kSmemTwoPerSm : static_cast<uint32_t>(kSmemLimit);
+        tinym_plan p{};
+        p.kernel = TINYM_KERNEL_TC;
+        p.mma_n = m <= 8 ? 8 : 16;
+        p.block_k = kBlockK;
+        p.split_k = 1;
+        p.stages = max_stages_fitting(p, limit);
+        const int max_st = p.stages;
+        const int64_t slots = static_cast<int64_t>(per_sm) * sm_count;
+        for (int s = 2; s <= kMaxSplit; ++s) {
+            if (tiles * s > slots) break;
+            const int64_t per = (kb + s - 1) / s;
+            if (per < 2 || (s - 1) * per >= kb) continue;
+            if (tc_stages_for(s, per, p.mma_n, max_st) < 0) continue;
+            p.split_k = s;
+        }
+        p.stages = tc_stages_for(p.split_k, (kb + p.split_k - 1) / p.split_k, p.mma_n, max_st);
+        const double fill = static_cast<double>(std::min<int64_t>(tiles * p.split_k, slots)) /
+                            static_cast<double>(slots);
+        if (fill > best_fill + 1e-9) {
+            best = p;
+            best_fill = fill;
+        }
+    }
+    return best;
+}
+
+// Kernel entry for a plan; sets the shared-memory opt-in once per device.
+int kernel_for(const tinym_plan& p, DeviceInfo* di, const void** fn) {
+    uint32_t attr_bit = 0;
+    if (p.kernel == TINYM_KERNEL_TC) {
+        *fn = p.mma_n == 8 ? reinterpret_cast<const void*>(&tinym::tinym_tc_kernel<8>)
+                           : reinterpret_cast<const void*>(&tinym::tinym_tc_kernel<16>);
+        attr_bit = p.mma_n == 8 ? 1u : 2u;
+    } else {
+        *fn = p.consumer_warps == 4 ? reinterpret_cast<const void*>(&tinym::tinym_simt_m1_kernel<4>)
+                                    : reinterpret_cast<const void*>(&tinym::tinym_simt_m1_kernel<8>);
+        attr_bit = p.consumer_warps == 4 ? 4u : 8u;
+    }
+    if (!(di->attr_done.load(std::memory_order_acquire) & attr_bit)) {
+        cudaError_t e = cudaFuncSetAttribute(*fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
+        if (p.split_k > kMaxSplit) {
+            e = cudaFuncSetAttribute(*fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(NonPortableClusterSize)");
+        }
+        di->attr_done.fetch_or(attr_bit, std::memory_order_acq_rel);
+    }
+    return TINYM_OK;
+}
+
+// Grid (split_k x tiles_n), block, shared memory and cluster attribute.
+void launch_config(const tinym_plan& p, void* stream, cudaLaunchConfig_t* cfg,
+                   cudaLaunchAttribute* attrs) {
+    *cfg = cudaLaunchConfig_t{};
+    cfg->gridDim = dim3(static_cast<unsigned>(p.split_k), static_cast<unsigned>(p.tiles_n), 1);
+    cfg->blockDim = dim3(static_cast<unsigned>(p.threads), 1, 1);
+    cfg->dynamicSmemBytes = static_cast<size_t>(p.smem_bytes);
+    cfg->stream = static_cast<cudaStream_t>(stream);
+    cfg->numAttrs = 0;
+    if (p.split_k > 1) {
+        attrs[0].id = cudaLaunchAttributeClusterDimension;
+        attrs[0].val.clusterDim.x = static_cast<unsigned>(p.split_k);
+        attrs[0].val.clusterDim.y = 1;
+        attrs[0].val.clusterDim.z = 1;
+        cfg->attrs = attrs;
+        cfg->numAttrs = 1;
+    }
+}
+
+// How many clusters of this plan can be resident at once (cached).
+struct ClusterOccEntry {
+    const void* fn;
+    int32_t split, smem, value;
+};
+constexpr int kOccCacheSize = 64;
+ClusterOccEntry g_occ[kMaxDevices][kOccCacheSize];
+int g_occ_used[kMaxDevices];
+std::mutex g_occ_mu;
+
+int max_active_clusters(const tinym_plan& p, int dev, DeviceInfo* di, int* out) {
+    const void* fn = nullptr;
+    int st = kernel_for(p, di, &fn);
+    if (st != TINYM_OK) return st;
+    {
+        std::lock_guard<std::mutex> lk(g_occ_mu);
+        for (int i = 0; i < g_occ_used[dev]; ++i) {
+            const ClusterOccEntry& e = g_occ[dev][i];
+            if (e.fn == fn && e.split == p.split_k && e.smem == p.smem_bytes) {
+                *out = e.value;
+                return TINYM_OK;
+            }
+        }
+    }
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attrs[1];
+    launch_config(p, nullptr, &cfg, attrs);
+    int n = 0;
+    if (p.split_k > 1) {
+        cudaError_t e = cudaOccupancyMaxActiveClusters(&n, fn, &cfg);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
+    } else {
+        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, p.threads,
+                                                                      static_cast<size_t>(p.smem_bytes));
+        if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+        n *= di->sm_count;
+    }
+    std::lock_guard<std::mutex> lk(g_occ_mu);
+    if (g_occ_used[dev] < kOccCacheSize) g_occ[dev][g_occ_used[dev]++] = {fn, p.split_k, p.smem_bytes, n};
+    *out = n;
+    return TINYM_OK;
 }
 
 }  // namespace
@@ -303,20 +436,13 @@ int tinym_select_plan(int64_t m, int64_t n, int64_t k, int32_t sm_count, tinym_p
     if (st != TINYM_OK) return st;
     const int64_t tiles = (n + kTileRows - 1) / kTileRows;
     const int64_t kb = (k + kBlockK - 1) / kBlockK;
-    tinym_plan p{};
-    p.kernel = TINYM_KERNEL_TC;
-    p.mma_n = m <= 8 ? 8 : 16;
-    p.block_k = kBlockK;
-    p.split_k = heuristic_split(tiles, kb, sm_count);
-    p.stages = 2;
-    p.stages = std::min<int64_t>(max_stages_fitting(p, m), std::max<int64_t>(2, (kb + p.split_k - 1) / p.split_k));
-    *out = p;
+    *out = heuristic_plan(m, tiles, kb, sm_count);
     return fill_derived(m, n, k, out);
 }
 
-int tinym_fp8_gemm_ex(const void* x, const void* w, void* y, int64_t ldy, int64_t m, int64_t n,
-                      int64_t k, const float* alpha_dev, float alpha, const tinym_plan* plan,
-                      void* stream) {
+static int gemm_impl(const void* x, const void* w, void* y, int64_t ldy, int64_t m, int64_t n,
+                     int64_t k, const float* alpha_dev, float alpha, const tinym_plan* plan,
+                     void* stream, uint32_t flags, uint64_t timeout_ns) {
     t_last_error[0] = '\0';
     if (!x || !w || !y) return fail(TINYM_ERR_INVALID_ARGUMENT, "X, W and Y must be non-null");
     int st = check_shape(m, n, k);
@@ -338,8 +464,21 @@ int tinym_fp8_gemm_ex(const void* x, const void* w, void* y, int64_t ldy, int64_
     if (plan) {
         p = *plan;
         if ((st = fill_derived(m, n, k, &p)) != TINYM_OK) return st;
-    } else if ((st = tinym_select_plan(m, n, k, di->sm_count, &p)) != TINYM_OK) {
-        return st;
+    } else {
+        if ((st = tinym_select_plan(m, n, k, di->sm_count, &p)) != TINYM_OK) return st;
+        // The table assumes every cluster of the grid is resident at once;
+        // shrink the K split until the device confirms that it is.
+        while (p.split_k > 1) {
+            int clusters = 0;
+            if ((st = max_active_clusters(p, dev, di, &clusters)) != TINYM_OK) return st;
+            if (clusters >= p.tiles_n) break;
+            --p.split_k;
+            const int64_t kb = (k + kBlockK - 1) / kBlockK;
+            const int s2 = tc_stages_for(p.split_k, (kb + p.split_k - 1) / p.split_k, p.mma_n,
+                                         kMaxStages);
+            if (s2 > 0) p.stages = std::max(p.stages, s2);
+            if ((st = fill_derived(m, n, k, &p)) != TINYM_OK) return st;
+        }
     }
 
     CUtensorMap tm_w, tm_x;
@@ -362,44 +501,34 @@ int tinym_fp8_gemm_ex(const void* x, const void* w, void* y, int64_t ldy, int64_
     prm.kb_per_split = (prm.kb_total + p.split_k - 1) / p.split_k;
     prm.split = p.split_k;
     prm.stages = p.stages;
-    prm.timeout_ns = kDefaultTimeoutNs;
+    prm.flags = flags;
+    prm.timeout_ns = timeout_ns;
 
     const void* fn = nullptr;
-    uint32_t attr_bit = 0;
-    if (p.kernel == TINYM_KERNEL_TC) {
-        fn = p.mma_n == 8 ? reinterpret_cast<const void*>(&tinym::tinym_tc_kernel<8>)
-                          : reinterpret_cast<const void*>(&tinym::tinym_tc_kernel<16>);
-        attr_bit = p.mma_n == 8 ? 1u : 2u;
-    } else {
-        fn = p.consumer_warps == 4 ? reinterpret_cast<const void*>(&tinym::tinym_simt_m1_kernel<4>)
-                                   : reinterpret_cast<const void*>(&tinym::tinym_simt_m1_kernel<8>);
-        attr_bit = p.consumer_warps == 4 ? 4u : 8u;
-    }
-    if (!(di->attr_done.load(std::memory_order_acquire) & attr_bit)) {
-        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
-        di->attr_done.fetch_or(attr_bit, std::memory_order_acq_rel);
-    }
-
+    if ((st = kernel_for(p, di, &fn)) != TINYM_OK) return st;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(static_cast<unsigned>(p.split_k), static_cast<unsigned>(p.tiles_n), 1);
-    cfg.blockDim = dim3(static_cast<unsigned>(p.threads), 1, 1);
-    cfg.dynamicSmemBytes = static_cast<size_t>(p.smem_bytes);
-    cfg.stream = static_cast<cudaStream_t>(stream);
     cudaLaunchAttribute attrs[1];
-    cfg.numAttrs = 0;
-    if (p.split_k > 1) {
-        attrs[0].id = cudaLaunchAttributeClusterDimension;
-        attrs[0].val.clusterDim.x = static_cast<unsigned>(p.split_k);
-        attrs[0].val.clusterDim.y = 1;
-        attrs[0].val.clusterDim.z = 1;
-        cfg.attrs = attrs;
-        cfg.numAttrs = 1;
-    }
+    launch_config(p, stream, &cfg, attrs);
     void* args[3] = {&tm_w, &tm_x, &prm};
     e = cudaLaunchKernelExC(&cfg, fn, args);
     if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
     return TINYM_OK;
+}
+
+int tinym_fp8_gemm_ex(const void* x, const void* w, void* y, int64_t ldy, int64_t m, int64_t n,
+                      int64_t k, const float* alpha_dev, float alpha, const tinym_plan* plan,
+                      void* stream) {
+    return gemm_impl(x, w, y, ldy, m, n, k, alpha_dev, alpha, plan, stream, 0u,
+                     kDefaultTimeoutNs);
+}
+
+int tinym_selftest_wait_timeout(const void* x, const void* w, void* y, int64_t m, int64_t n,
+                                int64_t k, const tinym_plan* plan, uint64_t timeout_ns,
+                                void* stream) {
+    if (timeout_ns == 0 || timeout_ns > 10ull * kDefaultTimeoutNs)
+        return fail(TINYM_ERR_INVALID_ARGUMENT, "timeout_ns must be in 1 .. 1e10");
+    return gemm_impl(x, w, y, n, m, n, k, nullptr, 1.0f, plan, stream,
+                     tinym::kFlagInjectNoLoads, timeout_ns);
 }
 
 int tinym_fp8_gemm(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k,
@@ -411,6 +540,25 @@ int tinym_fp8_gemm_dev_alpha(const void* x, const void* w, void* y, int64_t m, i
                              int64_t k, const float* alpha_dev, void* stream) {
     if (!alpha_dev) return fail(TINYM_ERR_INVALID_ARGUMENT, "alpha_dev must be non-null");
     return tinym_fp8_gemm_ex(x, w, y, n, m, n, k, alpha_dev, 0.0f, nullptr, stream);
+}
+
+int tinym_plan_max_active_clusters(int64_t m, int64_t n, int64_t k, const tinym_plan* plan,
+                                   int32_t* out) {
+    t_last_error[0] = '\0';
+    if (!plan || !out) return fail(TINYM_ERR_INVALID_ARGUMENT, "plan and out must be non-null");
+    int st = check_shape(m, n, k);
+    if (st != TINYM_OK) return st;
+    tinym_plan p = *plan;
+    if ((st = fill_derived(m, n, k, &p)) != TINYM_OK) return st;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    DeviceInfo* di = nullptr;
+    if ((st = device_info(dev, &di)) != TINYM_OK) return st;
+    int v = 0;
+    if ((st = max_active_clusters(p, dev, di, &v)) != TINYM_OK) return st;
+    *out = v;
+    return TINYM_OK;
 }
 
 int tinym_device_status(uint32_t* flags, int32_t clear) {

@@ -39,12 +39,24 @@ namespace tinym {
 // Device error word (one per device; read by tinym_device_status).
 __device__ uint32_t g_err_word;
 
+// Timeline trace points.  They compile to nothing unless a diagnostic build
+// defines TINYM_TRACE_POINTS, in which case the %globaltimer value of each
+// event is recorded per CTA in g_trace (latency analysis only; the shipped
+// library never defines it).
+#ifdef TINYM_TRACE_POINTS
+__device__ uint64_t g_trace[8192][16];
+#define TINYM_TRACE(id) (g_trace[blockIdx.y * gridDim.x + blockIdx.x][(id)] = globaltimer_ns())
+#else
+#define TINYM_TRACE(id) ((void)0)
+#endif
+
 enum : uint32_t {
     kErrProducerWait = 1u << 0,
     kErrMmaWait = 1u << 1,
     kErrEpilogueWait = 1u << 2,
     kErrDrain = 1u << 3,
     kErrConsumerWait = 1u << 4,
+    kErrReduceWait = 1u << 5,
 };
 
 constexpr int kTileRows = 128;   // W rows per tile (= MMA M)
@@ -62,24 +74,33 @@ struct TinymParams {
     int32_t kb_per_split;  // K blocks per CTA (last CTA of a cluster may get fewer)
     int32_t split;         // CTAs per tile (cluster size along x)
     int32_t stages;
-    uint64_t timeout_ns;
+    uint32_t flags;        // kFlag* bits (0 in normal operation)
+    uint64_t timeout_ns;   // limit of every mbarrier wait
 };
+
+// TinymParams::flags.  kFlagInjectNoLoads makes the producer issue no TMA
+// copies: nothing ever completes the full barriers, the consumers' bounded
+// waits run out, and the kernel reports through g_err_word and exits
+// cleanly.  Used only by the failure-detection self-test.
+constexpr uint32_t kFlagInjectNoLoads = 1u;
 
 // Shared-memory carve-up, identical on host (size) and device (offsets).
 struct SmemLayout {
     uint32_t w_off, x_off, red_off, bar_off, misc_off, bytes;
 };
 
+// red_rank_bytes: split-K partial-sum bytes one non-leader CTA sends to the
+// cluster leader (the leader reserves (split - 1) of them).
 __host__ __device__ inline SmemLayout smem_layout(int stages, int x_stage_bytes, int split,
-                                                  int m) {
+                                                  int red_rank_bytes) {
     SmemLayout L;
     L.w_off = 0;
     L.x_off = L.w_off + static_cast<uint32_t>(stages) * kWStageBytes;
     L.red_off = L.x_off + static_cast<uint32_t>(stages * x_stage_bytes);
     L.red_off = (L.red_off + 15u) & ~15u;
-    const uint32_t red_bytes = static_cast<uint32_t>((split - 1) * m * kTileRows * 4);
+    const uint32_t red_bytes = static_cast<uint32_t>((split - 1) * red_rank_bytes);
     L.bar_off = (L.red_off + red_bytes + 7u) & ~7u;
-    L.misc_off = L.bar_off + static_cast<uint32_t>(2 * stages + 1) * 8u;
+    L.misc_off = L.bar_off + static_cast<uint32_t>(2 * stages + 2) * 8u;
     // +1024: the dynamic window is re-aligned to 1024 bytes in the kernel.
     L.bytes = L.misc_off + 16u + 1024u;
     return L;
@@ -90,8 +111,19 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
     return p + (((a + 1023u) & ~1023u) - a);
 }
 
-// Output for one W row n of the tile: either stored (split == 1), pushed to
-// the cluster leader (rank > 0), or kept for the leader's reduction.
+// Row stride (FP32 elements) of the split-K partial blocks the TC kernel's
+// non-leader CTAs send to their cluster leader: MMA_N values padded by 4 so
+// that the leader's 16-byte shared-memory reads are bank-conflict free.
+__host__ __device__ constexpr int tc_red_stride(int mma_n) { return mma_n + 4; }
+__host__ __device__ constexpr int tc_red_rank_bytes(int mma_n) {
+    return kTileRows * tc_red_stride(mma_n) * 4;
+}
+
+// Named barrier 1 over the 128 epilogue threads (warps 2..5) of the TC kernel.
+__device__ __forceinline__ void epilogue_bar_sync() {
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
 __device__ __forceinline__ float load_alpha(const TinymParams& p) {
     return p.alpha_ptr ? __ldg(p.alpha_ptr) : p.alpha;
 }
@@ -107,10 +139,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     constexpr int kXStageBytes = MMA_N * kBlockK;  // 1 or 2 KiB, 1024-aligned
     constexpr uint32_t kStageTx = kWStageBytes + kXStageBytes;
     constexpr uint32_t kIdesc = idesc_e4m3_f32(kTileRows, MMA_N);
+    constexpr int kRedStride = tc_red_stride(MMA_N);
+    constexpr int kRedRankBytes = kTileRows * kRedStride * 4;  // per-rank block in the ring
+    constexpr int kRedSendBytes = kTileRows * MMA_N * 4;       // bytes a rank actually sends
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
-    const SmemLayout L = smem_layout(p.stages, kXStageBytes, p.split, p.m);
+    const SmemLayout L = smem_layout(p.stages, kXStageBytes, 1, 0);
     const uint32_t s_base = smem_u32(smem);
     const uint32_t w_ring = s_base + L.w_off;
     const uint32_t x_ring = s_base + L.x_off;
@@ -119,17 +154,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (stages + s); };
     const uint32_t acc_bar = bars + 8u * (2 * stages);
+    const uint32_t red_bar = bars + 8u * (2 * stages + 1);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.misc_off);
     volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L.misc_off + 4);
-    float* red = reinterpret_cast<float*>(smem + L.red_off);
+    // After the mainloop the rings are reused: the leader's W ring receives
+    // the other ranks' partial sums, the X ring stages the BF16 output tile.
+    float* red = reinterpret_cast<float*>(smem + L.w_off);
+    __nv_bfloat16* ystage = reinterpret_cast<__nv_bfloat16*>(smem + L.x_off);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int split_idx = blockIdx.x;
     const int tile = blockIdx.y;
+    const bool clustered = p.split > 1;
+    const bool leader = split_idx == 0;
     const int kb0 = split_idx * p.kb_per_split;
     const int kb1 = min(kb0 + p.kb_per_split, p.kb_total);
     const int nkb = kb1 - kb0;  // >= 1 by construction of the plan
+    // Fault injection (self-test only): issue no copies, so the consumers'
+    // bounded waits run out and report through the error word.
+    const int n_issue = (p.flags & kFlagInjectNoLoads) ? 0 : nkb;
 
     const WaitGuard guard{abort_flag, &g_err_word, p.timeout_ns};
 
@@ -146,6 +190,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tma_load_2d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), kc, 0, pol_x);
     };
     if (threadIdx.x == 0) {
+        TINYM_TRACE(0);
         tma_prefetch_desc(&tm_w);
         tma_prefetch_desc(&tm_x);
         for (int s = 0; s < stages; ++s) {
@@ -153,12 +198,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(empty_bar(s), 1);
         }
         mbar_init(acc_bar, 1);
+        mbar_init(red_bar, 1);
         *abort_flag = 0u;
         fence_mbar_init();
         fence_proxy_async_smem();
+        TINYM_TRACE(10);
         pol_w = l2_policy_w();
         pol_x = l2_policy_evict_last();
-        for (; issued < min(stages, nkb); ++issued) issue(issued);
+        for (; issued < min(stages, n_issue); ++issued) {
+            issue(issued);
+            if (issued == 0) TINYM_TRACE(11);
+        }
+        // Optional L2 prefetch of the boxes beyond the ring (build knob).
+        for (int j = issued; j < min(issued + TINYM_L2_PREFETCH_BOXES, n_issue); ++j)
+            tma_prefetch_l2_2d(&tm_w, (kb0 + j) * kBlockK, tile * kTileRows);
+        TINYM_TRACE(1);
+        // The cluster leader expects one partial-sum block from each other
+        // CTA of its cluster (st.async, completing bytes on red_bar).
+        if (clustered && leader) mbar_expect_tx(red_bar, (p.split - 1) * kRedSendBytes);
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(tmem_slot), kTmemCols);
@@ -168,21 +225,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     tc_fence_after_sync();
     const uint32_t tmem_d = *tmem_slot;
-    // Cluster phase 1: every CTA of the cluster has started (and set up its
-    // shared memory) before any CTA writes into another's shared memory.
-    if (p.split > 1) cluster_arrive_relaxed();
+    if (threadIdx.x == 0) TINYM_TRACE(2);
+    // Cluster barrier, one phase: it completes when every non-leader has
+    // started (they arrive now) and the leader's own MMAs have retired (it
+    // arrives after its mainloop), i.e. when the leader's W ring may be
+    // overwritten with partial sums.
+    if (clustered && !leader) cluster_arrive_relaxed();
 
     float acc[MMA_N];
     bool have_acc = false;
+    float alpha = 0.f;
 
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer (refills the ring as slots free up)
-            for (; issued < nkb; ++issued) {
+            for (; issued < n_issue; ++issued) {
                 const int s = issued % stages;
                 if (!mbar_wait(empty_bar(s), ((issued / stages) - 1) & 1, guard, kErrProducerWait))
                     break;
                 issue(issued);
+                // keep the L2 prefetch window TINYM_L2_PREFETCH_BOXES boxes ahead
+                if (TINYM_L2_PREFETCH_BOXES > 0 && issued + TINYM_L2_PREFETCH_BOXES < n_issue)
+                    tma_prefetch_l2_2d(&tm_w, (kb0 + issued + TINYM_L2_PREFETCH_BOXES) * kBlockK,
+                                       tile * kTileRows);
             }
             if (*abort_flag) {
                 // Drain the copies still in flight before shared memory is released.
@@ -196,6 +261,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int i = 0; i < nkb; ++i) {
                 const int s = i % stages;
                 if (!mbar_wait(full_bar(s), (i / stages) & 1, guard, kErrMmaWait)) break;
+                if (i == 0) TINYM_TRACE(3);
+                if (i == nkb - 1) TINYM_TRACE(4);
                 tc_fence_after_sync();
                 const uint32_t a0 = w_ring + s * kWStageBytes;
                 const uint32_t b0 = x_ring + s * kXStageBytes;
@@ -212,6 +279,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
     } else {
         // ---------------- epilogue warps 2..5: TMEM lanes 32*(warp%4) ..
+        alpha = load_alpha(p);  // issued early: its latency hides behind the mainloop
         // tcgen05.ld is .sync.aligned: the whole warp takes the same branch.
         const bool ready = mbar_wait(acc_bar, 0, guard, kErrEpilogueWait) && !*abort_flag;
         if (__all_sync(0xFFFFFFFFu, ready)) {
@@ -223,53 +291,93 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tmem_ld_x16(taddr, acc);
             }
             have_acc = true;
+            if (threadIdx.x == 64) TINYM_TRACE(5);
         }
     }
     __syncwarp();
 
-    // ---------------- output / split-K reduction
+    // ---------------- split-K reduction through distributed shared memory
     const int row = (warp & 3) * 32 + lane;  // W row within the tile (epilogue warps)
-    const int n_idx = tile * kTileRows + row;
-    if (p.split == 1) {
-        if (have_acc && n_idx < p.n) {
-            const float alpha = load_alpha(p);
-#pragma unroll
-            for (int m = 0; m < MMA_N; ++m)
-                if (m < p.m) p.y[static_cast<size_t>(m) * p.ldy + n_idx] = __float2bfloat16_rn(acc[m] * alpha);
-        }
-    } else {
-        __syncwarp();
-        cluster_wait_acquire();  // phase 1 complete: all CTAs of the cluster are resident
-        if (have_acc && split_idx > 0) {
-            const uint32_t remote = dsmem_map(smem_u32(red), 0);
-#pragma unroll
-            for (int m = 0; m < MMA_N; ++m)
-                if (m < p.m)
-                    dsmem_st_f32(remote + 4u * (((split_idx - 1) * p.m + m) * kTileRows + row),
-                                 acc[m]);
-        }
-        __syncwarp();
-        cluster_arrive_release();  // phase 2: partial sums are in the leader's shared memory
+    const bool epi = warp >= 2;
+    if (clustered) {
+        if (leader) cluster_arrive_release();  // leader's MMAs retired: ring is free
         cluster_wait_acquire();
-        if (have_acc && split_idx == 0 && n_idx < p.n) {
-            const float alpha = load_alpha(p);
+        if (threadIdx.x == 64) TINYM_TRACE(6);
+        if (epi && !leader) {
+            // Push this CTA's partial row block into the leader's ring,
+            // [rank-1][row][kRedStride].  Every epilogue thread always sends
+            // (zeros if it has no accumulator) so the leader's wait ends.
+            const uint32_t dst = dsmem_map(smem_u32(red), 0) +
+                                 static_cast<uint32_t>((split_idx - 1) * kRedRankBytes +
+                                                       row * kRedStride * 4);
+            const uint32_t rbar = dsmem_map(red_bar, 0);
 #pragma unroll
-            for (int m = 0; m < MMA_N; ++m) {
-                if (m < p.m) {
-                    float v = acc[m];  // K order: rank 0 first, then 1, 2, ...
-                    for (int r = 1; r < p.split; ++r) v += red[((r - 1) * p.m + m) * kTileRows + row];
-                    p.y[static_cast<size_t>(m) * p.ldy + n_idx] = __float2bfloat16_rn(v * alpha);
+            for (int c = 0; c < MMA_N; c += 4) {
+                float v[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) v[j] = have_acc ? acc[c + j] : 0.f;
+                st_async_v4(dst + 16u * (c / 4), v, rbar);
+            }
+        } else if (epi) {
+            // Leader: wait for every other rank's partials (bounded), then
+            // fold them into the accumulator in K order (rank 0 first), so
+            // the result does not depend on arrival order.
+            const bool got = mbar_drain(red_bar, 0, guard, kErrReduceWait);
+            if (threadIdx.x == 64) TINYM_TRACE(7);
+            if (got && have_acc) {
+                for (int r = 1; r < p.split; ++r) {
+                    const float4* part = reinterpret_cast<const float4*>(
+                        red + (r - 1) * (kRedRankBytes / 4) + row * kRedStride);
+#pragma unroll
+                    for (int c = 0; c < MMA_N / 4; ++c) {
+                        const float4 q = part[c];
+                        acc[4 * c + 0] += q.x;
+                        acc[4 * c + 1] += q.y;
+                        acc[4 * c + 2] += q.z;
+                        acc[4 * c + 3] += q.w;
+                    }
+                }
+            } else {
+                have_acc = false;
+            }
+            if (threadIdx.x == 64) TINYM_TRACE(12);
+        }
+    }
+
+    // ---------------- output: BF16 tile staged in shared memory, then
+    // written row by row with 16-byte stores (8 consecutive N per store).
+    if (epi && (!clustered || leader)) {
+        if (have_acc) {
+#pragma unroll
+            for (int m = 0; m < MMA_N; ++m)
+                ystage[m * kTileRows + row] = __float2bfloat16_rn(acc[m] * alpha);
+        }
+        epilogue_bar_sync();  // the 4 epilogue warps only
+        if (!*abort_flag) {
+            const int n0 = tile * kTileRows;
+            const bool vec = ((reinterpret_cast<uintptr_t>(p.y) & 15u) == 0) && (p.ldy % 8 == 0);
+            for (int c = row; c < p.m * (kTileRows / 8); c += kTileRows) {
+                const int m = c / (kTileRows / 8);
+                const int j = (c % (kTileRows / 8)) * 8;
+                const __nv_bfloat16* src = ystage + m * kTileRows + j;
+                __nv_bfloat16* dst = p.y + static_cast<size_t>(m) * p.ldy + n0 + j;
+                if (vec && n0 + j + 8 <= p.n) {
+                    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+                } else {
+                    for (int e = 0; e < 8 && n0 + j + e < p.n; ++e) dst[e] = src[e];
                 }
             }
         }
     }
 
     // ---------------- teardown
+    if (threadIdx.x == 64) TINYM_TRACE(8);
     tc_fence_before_sync();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after_sync();
         tmem_dealloc(tmem_d, kTmemCols);
+        if (threadIdx.x == 32) TINYM_TRACE(9);
     }
 }
 
@@ -288,7 +396,7 @@ __global__ void __launch_bounds__(32 * (CWARPS + 1), 1)
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
-    const SmemLayout L = smem_layout(p.stages, kXStageBytes, p.split, 1);
+    const SmemLayout L = smem_layout(p.stages, kXStageBytes, p.split, kTileRows * 4);
     const uint32_t s_base = smem_u32(smem);
     const uint32_t w_ring = s_base + L.w_off;
     const uint32_t x_ring = s_base + L.x_off;
@@ -306,6 +414,7 @@ __global__ void __launch_bounds__(32 * (CWARPS + 1), 1)
     const int kb0 = split_idx * p.kb_per_split;
     const int kb1 = min(kb0 + p.kb_per_split, p.kb_total);
     const int nkb = kb1 - kb0;
+    const int n_issue = (p.flags & kFlagInjectNoLoads) ? 0 : nkb;
 
     const WaitGuard guard{abort_flag, &g_err_word, p.timeout_ns};
 
@@ -330,7 +439,7 @@ __global__ void __launch_bounds__(32 * (CWARPS + 1), 1)
         fence_proxy_async_smem();
         pol_w = l2_policy_w();
         pol_x = l2_policy_evict_last();
-        for (; issued < min(stages, nkb); ++issued) issue(issued);  // first ring-full
+        for (; issued < min(stages, n_issue); ++issued) issue(issued);  // first ring-full
     }
     __syncthreads();
     if (p.split > 1) cluster_arrive_relaxed();
@@ -345,7 +454,7 @@ __global__ void __launch_bounds__(32 * (CWARPS + 1), 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            for (; issued < nkb; ++issued) {
+            for (; issued < n_issue; ++issued) {
                 const int s = issued % stages;
                 if (!mbar_wait(empty_bar(s), ((issued / stages) - 1) & 1, guard, kErrProducerWait))
                     break;

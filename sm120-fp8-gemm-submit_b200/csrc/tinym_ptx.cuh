@@ -130,6 +130,21 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// Prefetch a 2-D tensor box into L2 only (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int32_t c0,
+                                                   int32_t c1) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(c0), "r"(c1)
+                 : "memory");
+}
+
+// Build-time tuning knob: how many W boxes ahead of the shared-memory ring
+// the producer prefetches into L2 (0 = no prefetch).
+#ifndef TINYM_L2_PREFETCH_BOXES
+#define TINYM_L2_PREFETCH_BOXES 0
+#endif
+
 // L2 eviction policies for the streamed weight (read once) and the
 // activation (re-read by every CTA).
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
@@ -261,6 +276,18 @@ __device__ __forceinline__ uint32_t dsmem_map(uint32_t local_addr, uint32_t rank
 __device__ __forceinline__ void dsmem_st_f32(uint32_t cluster_addr, float v) {
     asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
 }
+// Asynchronous 16-byte store into another CTA's shared memory (cluster
+// address from dsmem_map); its bytes complete on the mbarrier at the
+// cluster address `remote_bar` in the destination CTA.
+__device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, const float (&v)[4],
+                                            uint32_t remote_bar) {
+    asm volatile(
+        "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, "
+        "[%5];" ::"r"(cluster_addr),
+        "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "r"(remote_bar)
+        : "memory");
+}
+
 __device__ __forceinline__ void cluster_arrive_relaxed() {
     asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }

@@ -49,6 +49,8 @@ EXPORTED = (
     "tinym_select_plan",
     "tinym_check_plan",
     "tinym_device_status",
+    "tinym_plan_max_active_clusters",
+    "tinym_selftest_wait_timeout",
     "tinym_status_string",
     "tinym_last_error",
     "tinym_abi_version",
@@ -115,6 +117,12 @@ def capi() -> ctypes.CDLL:
             lib.tinym_check_plan.restype = ctypes.c_int
             lib.tinym_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int32]
             lib.tinym_device_status.restype = ctypes.c_int
+            lib.tinym_selftest_wait_timeout.argtypes = [vp, vp, vp, i64, i64, i64,
+                                                        ctypes.POINTER(Plan), ctypes.c_uint64, vp]
+            lib.tinym_selftest_wait_timeout.restype = ctypes.c_int
+            lib.tinym_plan_max_active_clusters.argtypes = [i64, i64, i64, ctypes.POINTER(Plan),
+                                                           ctypes.POINTER(ctypes.c_int32)]
+            lib.tinym_plan_max_active_clusters.restype = ctypes.c_int
             lib.tinym_status_string.argtypes = [ctypes.c_int32]
             lib.tinym_status_string.restype = ctypes.c_char_p
             lib.tinym_last_error.argtypes = []
@@ -177,6 +185,13 @@ def gemm_ptr(x_ptr: int, w_ptr: int, y_ptr: int, m: int, n: int, k: int, *,
     st = lib.tinym_fp8_gemm_ex(x_ptr, w_ptr, y_ptr, n if ldy is None else ldy, m, n, k,
                                alpha_ptr, alpha, pl, stream)
     _check(st)
+
+
+def max_active_clusters(m: int, n: int, k: int, plan: Plan) -> int:
+    """Clusters of `plan` the current GPU can hold resident at once."""
+    out = ctypes.c_int32(0)
+    _check(capi().tinym_plan_max_active_clusters(m, n, k, ctypes.byref(plan), ctypes.byref(out)))
+    return int(out.value)
 
 
 def device_status(clear: bool = True) -> int:

@@ -54,12 +54,13 @@ def test_plan_struct_layout():
 @pytest.mark.parametrize("m,k,n", OFFICIAL)
 def test_dispatch_table_official_points(m, k, n):
     """Every official point gets a plan that fits 227 KiB of shared memory and
-    one wave on 148 SMs."""
+    one wave on 148 SMs (two CTAs per SM when each fits half an SM's 228 KiB)."""
     import tinym_b200
 
     p = tinym_b200.select_plan(m, n, k, 148)
-    assert p.grid_ctas <= 148
     assert p.smem_bytes <= 232448
+    per_sm = 2 if p.smem_bytes <= (233472 - 2048) // 2 else 1
+    assert p.grid_ctas <= per_sm * 148
     assert p.tiles_n == (n + 127) // 128
     kb = (k + 127) // 128
     per = -(-kb // p.split_k)
@@ -74,7 +75,7 @@ def test_dispatch_fills_small_sm_counts():
     import tinym_b200
 
     p = tinym_b200.select_plan(9, 5120, 6144, 40)
-    assert p.grid_ctas <= 40 or p.split_k == 1
+    assert p.grid_ctas <= 2 * 40 or p.split_k == 1
     p = tinym_b200.select_plan(1, 128, 128, 148)
     assert p.split_k == 1  # one K block cannot be split
 
@@ -160,3 +161,15 @@ def test_candidate_kernel_surface():
     with pytest.raises(ValueError):
         candidate_kernel.prepare_weights(torch.zeros(4, 4))
     assert candidate_kernel.build() is True
+
+
+@pytest.mark.parametrize("m", [1, 3, 9, 16])
+def test_dispatch_plans_always_validate(m):
+    """The dispatch table never emits a plan its own validator rejects."""
+    import tinym_b200
+
+    for k in (16, 48, 128, 144, 272, 1040, 2064, 4096, 5120, 6144, 8192):
+        for n in (1, 127, 129, 300, 640, 1000, 4100, 5120, 8192, 16384):
+            for sms in (148, 132, 40):
+                p = tinym_b200.select_plan(m, n, k, sms)
+                tinym_b200.check_plan(m, n, k, p)

@@ -119,10 +119,10 @@ int device_info(int dev, DeviceInfo** out) {
 struct MapKey {
     const void* ptr;
     int64_t rows, cols;
-    int32_t box_rows, swizzle, dev;
+    int32_t box_rows, swizzle, chunks, dev;
     bool operator==(const MapKey& o) const {
         return ptr == o.ptr && rows == o.rows && cols == o.cols && box_rows == o.box_rows &&
-               swizzle == o.swizzle && dev == o.dev;
+               swizzle == o.swizzle && chunks == o.chunks && dev == o.dev;
     }
 };
 struct MapEntry {
@@ -137,10 +137,14 @@ uint64_t g_map_clock = 0;
 std::mutex g_map_mu;
 
 // Encodes (or fetches) the map of a row-major [rows, cols] uint8 matrix read
-// in boxes of [box_rows, 128 bytes]; swizzle 1 = 128B, 0 = none.
-int get_map(const void* ptr, int64_t rows, int64_t cols, int box_rows, int swizzle, int dev,
-            CUtensorMap* out) {
-    const MapKey key{ptr, rows, cols, box_rows, swizzle, dev};
+// in boxes of `chunks` x [box_rows, 128 bytes]; swizzle 1 = 128B, 0 = none.
+// chunks == 1: a 2-D map {cols, rows}.  chunks > 1 (cols % 128 == 0): a 3-D
+// view {128, rows, cols / 128} with strides {cols, 128} whose box
+// {128, box_rows, chunks} lands as `chunks` consecutive [box_rows x 128 B]
+// tiles -- several K chunks per TMA instruction.
+int get_map(const void* ptr, int64_t rows, int64_t cols, int box_rows, int swizzle, int chunks,
+            int dev, CUtensorMap* out) {
+    const MapKey key{ptr, rows, cols, box_rows, swizzle, chunks, dev};
     std::lock_guard<std::mutex> lk(g_map_mu);
     MapEntry* victim = &g_maps[0];
     for (auto& e : g_maps) {
@@ -156,13 +160,28 @@ int get_map(const void* ptr, int64_t rows, int64_t cols, int box_rows, int swizz
     if (!encode)
         return fail(TINYM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (%s)",
                     cudaGetErrorString(g_encode_err));
-    cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-    cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols)};
-    cuuint32_t box[2] = {static_cast<cuuint32_t>(kBlockK), static_cast<cuuint32_t>(box_rows)};
-    cuuint32_t estr[2] = {1, 1};
+    const bool three = chunks > 1;
+    cuuint64_t dims[3], strides[2];
+    cuuint32_t box[3], estr[3] = {1, 1, 1};
+    if (!three) {
+        dims[0] = static_cast<cuuint64_t>(cols);
+        dims[1] = static_cast<cuuint64_t>(rows);
+        strides[0] = static_cast<cuuint64_t>(cols);
+        box[0] = static_cast<cuuint32_t>(kBlockK);
+        box[1] = static_cast<cuuint32_t>(box_rows);
+    } else {
+        dims[0] = static_cast<cuuint64_t>(kBlockK);
+        dims[1] = static_cast<cuuint64_t>(rows);
+        dims[2] = static_cast<cuuint64_t>(cols / kBlockK);
+        strides[0] = static_cast<cuuint64_t>(cols);
+        strides[1] = static_cast<cuuint64_t>(kBlockK);
+        box[0] = static_cast<cuuint32_t>(kBlockK);
+        box[1] = static_cast<cuuint32_t>(box_rows);
+        box[2] = static_cast<cuuint32_t>(chunks);
+    }
     CUtensorMap map;
-    CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims,
-                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+    CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, three ? 3 : 2, const_cast<void*>(ptr),
+                        dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                         TINYM_L2_PROMOTION, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
@@ -179,24 +198,35 @@ int get_map(const void* ptr, int64_t rows, int64_t cols, int box_rows, int swizz
 }
 
 // ---------------------------------------------------------------- plans
+int plan_chunks(const tinym_plan& p) { return p.block_k / kBlockK; }
+
+int w_stage_bytes(const tinym_plan& p) { return plan_chunks(p) * tinym::kWStageBytes; }
+
 int x_stage_bytes(const tinym_plan& p) {
-    return p.kernel == TINYM_KERNEL_TC ? p.mma_n * kBlockK : kBlockK;
+    return p.kernel == TINYM_KERNEL_TC ? plan_chunks(p) * p.mma_n * kBlockK : kBlockK;
 }
 
 // Dynamic shared memory of a plan.  The TC kernel receives split-K partials
 // in its W ring (no separate buffer); the SIMT kernel keeps a separate
 // (split - 1) x 128-float buffer.
 uint32_t plan_smem_bytes(const tinym_plan& p) {
-    if (p.kernel == TINYM_KERNEL_TC) return tinym::smem_layout(p.stages, x_stage_bytes(p), 1, 0).bytes;
-    return tinym::smem_layout(p.stages, x_stage_bytes(p), p.split_k, kTileRows * 4).bytes;
+    if (p.kernel == TINYM_KERNEL_TC)
+        return tinym::smem_layout(p.stages, w_stage_bytes(p), x_stage_bytes(p), 1, 0).bytes;
+    return tinym::smem_layout(p.stages, w_stage_bytes(p), x_stage_bytes(p), p.split_k,
+                              kTileRows * 4).bytes;
 }
 
 int fill_derived(int64_t m, int64_t n, int64_t k, tinym_plan* p) {
     const int64_t tiles = (n + kTileRows - 1) / kTileRows;
-    const int64_t kb = (k + kBlockK - 1) / kBlockK;
     if (p->kernel != TINYM_KERNEL_TC && p->kernel != TINYM_KERNEL_SIMT_M1)
         return fail(TINYM_ERR_BAD_PLAN, "plan.kernel %d is not a kernel family", p->kernel);
-    if (p->block_k != kBlockK) return fail(TINYM_ERR_BAD_PLAN, "plan.block_k must be %d", kBlockK);
+    if (p->block_k != 128 && p->block_k != 256 && p->block_k != 512)
+        return fail(TINYM_ERR_BAD_PLAN, "plan.block_k must be 128, 256 or 512");
+    if (p->block_k != kBlockK && (p->kernel != TINYM_KERNEL_TC || k % kBlockK != 0))
+        return fail(TINYM_ERR_BAD_PLAN,
+                    "plan.block_k > 128 needs the TC kernel and K %% 128 == 0 (K = %lld)",
+                    (long long)k);
+    const int64_t kb = (k + p->block_k - 1) / p->block_k;  // K stages
     if (p->kernel == TINYM_KERNEL_TC) {
         if (p->mma_n != 8 && p->mma_n != 16)
             return fail(TINYM_ERR_BAD_PLAN, "plan.mma_n must be 8 or 16");
@@ -224,7 +254,7 @@ int fill_derived(int64_t m, int64_t n, int64_t k, tinym_plan* p) {
         return fail(TINYM_ERR_BAD_PLAN, "plan needs %u bytes of shared memory (> %d)", smem,
                     kSmemLimit);
     if (p->kernel == TINYM_KERNEL_TC &&
-        (p->split_k - 1) * tinym::tc_red_rank_bytes(p->mma_n) > p->stages * tinym::kWStageBytes)
+        (p->split_k - 1) * tinym::tc_red_rank_bytes(p->mma_n) > p->stages * w_stage_bytes(*p))
         return fail(TINYM_ERR_BAD_PLAN,
                     "split_k %d needs %d bytes of partial sums, more than the %d-stage ring holds",
                     p->split_k, (p->split_k - 1) * tinym::tc_red_rank_bytes(p->mma_n), p->stages);
@@ -253,9 +283,9 @@ int check_shape(int64_t m, int64_t n, int64_t k) {
 // Ring depth for a TC plan: enough stages to cover the CTA's K blocks (no
 // more is useful) and to hold the split-K partials the leader receives in
 // its ring, at most max_st; -1 if the partials cannot fit.
-int tc_stages_for(int split, int64_t kb_per_cta, int mma_n, int max_st) {
+int tc_stages_for(int split, int64_t kb_per_cta, int mma_n, int w_stage, int max_st) {
     const int red = (split - 1) * tinym::tc_red_rank_bytes(mma_n);
-    const int need_red = (red + tinym::kWStageBytes - 1) / tinym::kWStageBytes;
+    const int need_red = (red + w_stage - 1) / w_stage;
     const int64_t st = std::max<int64_t>({2, kb_per_cta < max_st ? kb_per_cta : max_st, need_red});
     return st > max_st ? -1 : static_cast<int>(st);
 }
@@ -272,54 +302,54 @@ int max_stages_fitting(const tinym_plan& p, uint32_t limit) {
     return st;
 }
 
-// Heuristic part of the dispatch table.  Tiled TMA streams saturate HBM
-// only with every SM busy, and a CTA alone cannot pull an SM's share, so
-// the search covers one and two CTAs per SM: for each, the largest K split
-// (cluster size <= 8) that keeps tiles * split CTAs within one wave, leaves
-// each CTA >= 2 K blocks and fits its partial sums in the ring.  The option
-// filling more of the GPU's CTA slots wins (ties: two CTAs per SM).
-tinym_plan heuristic_plan(int64_t m, int64_t tiles, int64_t kb, int sm_count) {
-    tinym_plan best{};
-    double best_fill = -1.0;
-    for (int per_sm = 2; per_sm >= 1; --per_sm) {
-        const uint32_t limit = per_sm == 2 ? kSmemTwoPerSm : static_cast<uint32_t>(kSmemLimit);
-        tinym_plan p{};
-        p.kernel = TINYM_KERNEL_TC;
-        p.mma_n = m <= 8 ? 8 : 16;
-        p.block_k = kBlockK;
-        p.split_k = 1;
-        p.stages = max_stages_fitting(p, limit);
-        const int max_st = p.stages;
-        const int64_t slots = static_cast<int64_t>(per_sm) * sm_count;
-        for (int s = 2; s <= kMaxSplit; ++s) {
-            if (tiles * s > slots) break;
-            const int64_t per = (kb + s - 1) / s;
-            if (per < 2 || (s - 1) * per >= kb) continue;
-            if (tc_stages_for(s, per, p.mma_n, max_st) < 0) continue;
-            p.split_k = s;
-        }
-        p.stages = tc_stages_for(p.split_k, (kb + p.split_k - 1) / p.split_k, p.mma_n, max_st);
-        const double fill = static_cast<double>(std::min<int64_t>(tiles * p.split_k, slots)) /
-                            static_cast<double>(slots);
-        if (fill > best_fill + 1e-9) {
-            best = p;
-            best_fill = fill;
-        }
+// Heuristic part of the dispatch table, fitted to B200 measurements of all
+// six official points (plan sweeps: one CTA per SM with a deep ring beat
+// two CTAs per SM everywhere; a CTA's TMA stream is bound by instructions,
+// so the widest stage wins):
+//  * block_k = 512 (one 64 KiB W box per TMA instruction) whenever
+//    K % 128 == 0, else 128 (2-D boxes; TMA zero-fills the K tail);
+//  * as many stages as fit 227 KiB;
+//  * the largest K split (cluster size <= 8) that keeps tiles * split CTAs
+//    within one CTA per SM and gives every CTA >= 2 stages.
+tinym_plan heuristic_plan(int64_t m, int64_t k, int64_t tiles, int sm_count) {
+    tinym_plan p{};
+    p.kernel = TINYM_KERNEL_TC;
+    p.mma_n = m <= 8 ? 8 : 16;
+    p.block_k = (k % kBlockK == 0) ? 4 * kBlockK : kBlockK;
+    p.split_k = 1;
+    const int64_t kb = (k + p.block_k - 1) / p.block_k;
+    const int max_st = max_stages_fitting(p, static_cast<uint32_t>(kSmemLimit));
+    for (int s = 2; s <= kMaxSplit; ++s) {
+        if (tiles * s > sm_count) break;
+        const int64_t per = (kb + s - 1) / s;
+        if (per < 2 || (s - 1) * per >= kb) continue;
+        if (tc_stages_for(s, per, p.mma_n, w_stage_bytes(p), max_st) < 0) continue;
+        p.split_k = s;
     }
-    return best;
+    p.stages = tc_stages_for(p.split_k, (kb + p.split_k - 1) / p.split_k, p.mma_n,
+                             w_stage_bytes(p), max_st);
+    return p;
 }
 
 // Kernel entry for a plan; sets the shared-memory opt-in once per device.
 int kernel_for(const tinym_plan& p, DeviceInfo* di, const void** fn) {
+    static const void* const kTc[2][3] = {
+        {reinterpret_cast<const void*>(&tinym::tinym_tc_kernel<8, 1>),
+         reinterpret_cast<const void*>(&tinym::tinym_tc_kernel<8, 2>),
+         reinterpret_cast<const void*>(&tinym::tinym_tc_kernel<8, 4>)},
+        {reinterpret_cast<const void*>(&tinym::tinym_tc_kernel<16, 1>),
+         reinterpret_cast<const void*>(&tinym::tinym_tc_kernel<16, 2>),
+         reinterpret_cast<const void*>(&tinym::tinym_tc_kernel<16, 4>)}};
     uint32_t attr_bit = 0;
     if (p.kernel == TINYM_KERNEL_TC) {
-        *fn = p.mma_n == 8 ? reinterpret_cast<const void*>(&tinym::tinym_tc_kernel<8>)
-                           : reinterpret_cast<const void*>(&tinym::tinym_tc_kernel<16>);
-        attr_bit = p.mma_n == 8 ? 1u : 2u;
+        const int ni = p.mma_n == 8 ? 0 : 1;
+        const int ci = p.block_k == 128 ? 0 : (p.block_k == 256 ? 1 : 2);
+        *fn = kTc[ni][ci];
+        attr_bit = 1u << (ni * 3 + ci);
     } else {
         *fn = p.consumer_warps == 4 ? reinterpret_cast<const void*>(&tinym::tinym_simt_m1_kernel<4>)
                                     : reinterpret_cast<const void*>(&tinym::tinym_simt_m1_kernel<8>);
-        attr_bit = p.consumer_warps == 4 ? 4u : 8u;
+        attr_bit = p.consumer_warps == 4 ? 1u << 6 : 1u << 7;
     }
     if (!(di->attr_done.load(std::memory_order_acquire) & attr_bit)) {
         cudaError_t e = cudaFuncSetAttribute(*fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
@@ -435,8 +465,7 @@ int tinym_select_plan(int64_t m, int64_t n, int64_t k, int32_t sm_count, tinym_p
     int st = check_shape(m, n, k);
     if (st != TINYM_OK) return st;
     const int64_t tiles = (n + kTileRows - 1) / kTileRows;
-    const int64_t kb = (k + kBlockK - 1) / kBlockK;
-    *out = heuristic_plan(m, tiles, kb, sm_count);
+    *out = heuristic_plan(m, k, tiles, sm_count);
     return fill_derived(m, n, k, out);
 }
 
@@ -473,20 +502,22 @@ static int gemm_impl(const void* x, const void* w, void* y, int64_t ldy, int64_t
             if ((st = max_active_clusters(p, dev, di, &clusters)) != TINYM_OK) return st;
             if (clusters >= p.tiles_n) break;
             --p.split_k;
-            const int64_t kb = (k + kBlockK - 1) / kBlockK;
+            const int64_t kb = (k + p.block_k - 1) / p.block_k;
+            const int max_st = max_stages_fitting(p, static_cast<uint32_t>(kSmemLimit));
             const int s2 = tc_stages_for(p.split_k, (kb + p.split_k - 1) / p.split_k, p.mma_n,
-                                         kMaxStages);
+                                         w_stage_bytes(p), max_st);
             if (s2 > 0) p.stages = std::max(p.stages, s2);
             if ((st = fill_derived(m, n, k, &p)) != TINYM_OK) return st;
         }
     }
 
     CUtensorMap tm_w, tm_x;
-    if ((st = get_map(w, n, k, kTileRows, 1, dev, &tm_w)) != TINYM_OK) return st;
+    const int chunks = plan_chunks(p);
+    if ((st = get_map(w, n, k, kTileRows, 1, chunks, dev, &tm_w)) != TINYM_OK) return st;
     if (p.kernel == TINYM_KERNEL_TC) {
-        if ((st = get_map(x, m, k, p.mma_n, 1, dev, &tm_x)) != TINYM_OK) return st;
+        if ((st = get_map(x, m, k, p.mma_n, 1, chunks, dev, &tm_x)) != TINYM_OK) return st;
     } else {
-        if ((st = get_map(x, m, k, 1, 0, dev, &tm_x)) != TINYM_OK) return st;
+        if ((st = get_map(x, m, k, 1, 0, 1, dev, &tm_x)) != TINYM_OK) return st;
     }
 
     TinymParams prm{};
@@ -497,7 +528,7 @@ static int gemm_impl(const void* x, const void* w, void* y, int64_t ldy, int64_t
     prm.n = static_cast<int32_t>(n);
     prm.k = static_cast<int32_t>(k);
     prm.ldy = static_cast<int32_t>(ldy);
-    prm.kb_total = static_cast<int32_t>((k + kBlockK - 1) / kBlockK);
+    prm.kb_total = static_cast<int32_t>((k + p.block_k - 1) / p.block_k);
     prm.kb_per_split = (prm.kb_total + p.split_k - 1) / p.split_k;
     prm.split = p.split_k;
     prm.stages = p.stages;

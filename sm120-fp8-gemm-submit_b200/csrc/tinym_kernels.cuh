@@ -60,8 +60,8 @@ enum : uint32_t {
 };
 
 constexpr int kTileRows = 128;   // W rows per tile (= MMA M)
-constexpr int kBlockK = 128;     // K bytes per stage (= one 128B swizzle row)
-constexpr int kWStageBytes = kTileRows * kBlockK;  // 16 KiB
+constexpr int kBlockK = 128;     // K bytes of one chunk (= one 128B swizzle row)
+constexpr int kWStageBytes = kTileRows * kBlockK;  // one W chunk: 16 KiB
 constexpr int kTcThreads = 192;  // warp0 TMA, warp1 MMA, warps2-5 epilogue
 constexpr int kTmemCols = 32;    // minimum allocation; MMA_N <= 16 columns used
 
@@ -70,8 +70,8 @@ struct TinymParams {
     const float* alpha_ptr;  // if non-null, alpha is read here on the device
     float alpha;
     int32_t m, n, k, ldy;
-    int32_t kb_total;      // ceil(K / 128)
-    int32_t kb_per_split;  // K blocks per CTA (last CTA of a cluster may get fewer)
+    int32_t kb_total;      // K stages: ceil(K / (128 * chunks per stage))
+    int32_t kb_per_split;  // K stages per CTA (last CTA of a cluster may get fewer)
     int32_t split;         // CTAs per tile (cluster size along x)
     int32_t stages;
     uint32_t flags;        // kFlag* bits (0 in normal operation)
@@ -91,11 +91,11 @@ struct SmemLayout {
 
 // red_rank_bytes: split-K partial-sum bytes one non-leader CTA sends to the
 // cluster leader (the leader reserves (split - 1) of them).
-__host__ __device__ inline SmemLayout smem_layout(int stages, int x_stage_bytes, int split,
-                                                  int red_rank_bytes) {
+__host__ __device__ inline SmemLayout smem_layout(int stages, int w_stage_bytes, int x_stage_bytes,
+                                                  int split, int red_rank_bytes) {
     SmemLayout L;
     L.w_off = 0;
-    L.x_off = L.w_off + static_cast<uint32_t>(stages) * kWStageBytes;
+    L.x_off = L.w_off + static_cast<uint32_t>(stages) * static_cast<uint32_t>(w_stage_bytes);
     L.red_off = L.x_off + static_cast<uint32_t>(stages * x_stage_bytes);
     L.red_off = (L.red_off + 15u) & ~15u;
     const uint32_t red_bytes = static_cast<uint32_t>((split - 1) * red_rank_bytes);
@@ -131,13 +131,21 @@ __device__ __forceinline__ float load_alpha(const TinymParams& p) {
 // =====================================================================
 // tcgen05 swap-AB kernel
 // =====================================================================
-template <int MMA_N>
+template <int MMA_N, int CHUNKS>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tinym_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
                     const __grid_constant__ CUtensorMap tm_x, const TinymParams p) {
     static_assert(MMA_N == 8 || MMA_N == 16, "MMA_N must be 8 or 16");
-    constexpr int kXStageBytes = MMA_N * kBlockK;  // 1 or 2 KiB, 1024-aligned
-    constexpr uint32_t kStageTx = kWStageBytes + kXStageBytes;
+    static_assert(CHUNKS == 1 || CHUNKS == 2 || CHUNKS == 4, "1, 2 or 4 K chunks per stage");
+    // One stage = CHUNKS K chunks of 128 bytes.  Each W chunk is a standard
+    // [128 rows x 128 B] 128B-swizzled tile (16 KiB), each X chunk
+    // [MMA_N rows x 128 B]; with CHUNKS > 1 one 3-D TMA box fetches all of
+    // a stage's chunks, which raises the bytes moved per TMA instruction
+    // (a single CTA's stream is bound by instructions, not bytes).
+    constexpr int kXChunkBytes = MMA_N * kBlockK;  // 1 or 2 KiB, 1024-aligned
+    constexpr int kWStage = CHUNKS * kWStageBytes;
+    constexpr int kXStageBytes = CHUNKS * kXChunkBytes;
+    constexpr uint32_t kStageTx = kWStage + kXStageBytes;
     constexpr uint32_t kIdesc = idesc_e4m3_f32(kTileRows, MMA_N);
     constexpr int kRedStride = tc_red_stride(MMA_N);
     constexpr int kRedRankBytes = kTileRows * kRedStride * 4;  // per-rank block in the ring
@@ -145,7 +153,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
-    const SmemLayout L = smem_layout(p.stages, kXStageBytes, 1, 0);
+    const SmemLayout L = smem_layout(p.stages, kWStage, kXStageBytes, 1, 0);
     const uint32_t s_base = smem_u32(smem);
     const uint32_t w_ring = s_base + L.w_off;
     const uint32_t x_ring = s_base + L.x_off;
@@ -184,10 +192,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t pol_w = 0, pol_x = 0;
     auto issue = [&](int i) {
         const int s = i % stages;
-        const int kc = (kb0 + i) * kBlockK;
+        const int chunk = (kb0 + i) * CHUNKS;  // first 128-byte K chunk of the stage
         mbar_expect_tx(full_bar(s), kStageTx);
-        tma_load_2d(w_ring + s * kWStageBytes, &tm_w, full_bar(s), kc, tile * kTileRows, pol_w);
-        tma_load_2d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), kc, 0, pol_x);
+        if constexpr (CHUNKS == 1) {
+            tma_load_2d(w_ring + s * kWStage, &tm_w, full_bar(s), chunk * kBlockK, tile * kTileRows,
+                        pol_w);
+            tma_load_2d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), chunk * kBlockK, 0, pol_x);
+        } else {
+            tma_load_3d(w_ring + s * kWStage, &tm_w, full_bar(s), 0, tile * kTileRows, chunk, pol_w);
+            tma_load_3d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), 0, 0, chunk, pol_x);
+        }
     };
     if (threadIdx.x == 0) {
         TINYM_TRACE(0);
@@ -209,9 +223,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             issue(issued);
             if (issued == 0) TINYM_TRACE(11);
         }
-        // Optional L2 prefetch of the boxes beyond the ring (build knob).
-        for (int j = issued; j < min(issued + TINYM_L2_PREFETCH_BOXES, n_issue); ++j)
-            tma_prefetch_l2_2d(&tm_w, (kb0 + j) * kBlockK, tile * kTileRows);
         TINYM_TRACE(1);
         // The cluster leader expects one partial-sum block from each other
         // CTA of its cluster (st.async, completing bytes on red_bar).
@@ -244,10 +255,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (!mbar_wait(empty_bar(s), ((issued / stages) - 1) & 1, guard, kErrProducerWait))
                     break;
                 issue(issued);
-                // keep the L2 prefetch window TINYM_L2_PREFETCH_BOXES boxes ahead
-                if (TINYM_L2_PREFETCH_BOXES > 0 && issued + TINYM_L2_PREFETCH_BOXES < n_issue)
-                    tma_prefetch_l2_2d(&tm_w, (kb0 + issued + TINYM_L2_PREFETCH_BOXES) * kBlockK,
-                                       tile * kTileRows);
             }
             if (*abort_flag) {
                 // Drain the copies still in flight before shared memory is released.
@@ -264,13 +271,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (i == 0) TINYM_TRACE(3);
                 if (i == nkb - 1) TINYM_TRACE(4);
                 tc_fence_after_sync();
-                const uint32_t a0 = w_ring + s * kWStageBytes;
-                const uint32_t b0 = x_ring + s * kXStageBytes;
 #pragma unroll
-                for (int kk = 0; kk < kBlockK / 32; ++kk) {
-                    umma_e4m3(tmem_d, sw128_kmajor_desc(a0 + kk * 32),
-                              sw128_kmajor_desc(b0 + kk * 32), kIdesc,
-                              (i > 0 || kk > 0) ? 1u : 0u);
+                for (int c = 0; c < CHUNKS; ++c) {
+                    const uint32_t a0 = w_ring + s * kWStage + c * kWStageBytes;
+                    const uint32_t b0 = x_ring + s * kXStageBytes + c * kXChunkBytes;
+#pragma unroll
+                    for (int kk = 0; kk < kBlockK / 32; ++kk) {
+                        umma_e4m3(tmem_d, sw128_kmajor_desc(a0 + kk * 32),
+                                  sw128_kmajor_desc(b0 + kk * 32), kIdesc,
+                                  (i > 0 || c > 0 || kk > 0) ? 1u : 0u);
+                    }
                 }
                 umma_commit(empty_bar(s));  // frees the slot once these MMAs retire
             }
@@ -396,7 +406,7 @@ __global__ void __launch_bounds__(32 * (CWARPS + 1), 1)
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
-    const SmemLayout L = smem_layout(p.stages, kXStageBytes, p.split, kTileRows * 4);
+    const SmemLayout L = smem_layout(p.stages, kWStageBytes, kXStageBytes, p.split, kTileRows * 4);
     const uint32_t s_base = smem_u32(smem);
     const uint32_t w_ring = s_base + L.w_off;
     const uint32_t x_ring = s_base + L.x_off;

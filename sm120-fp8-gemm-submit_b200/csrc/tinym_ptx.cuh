@@ -130,20 +130,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
-// Prefetch a 2-D tensor box into L2 only (no shared memory, no barrier).
-__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int32_t c0,
-                                                   int32_t c1) {
-    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                     reinterpret_cast<uint64_t>(map)),
-                 "r"(c0), "r"(c1)
-                 : "memory");
+// 3-D tiled bulk tensor copy global -> shared (this CTA); c0 innermost.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int32_t c0, int32_t c1, int32_t c2, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "l"(policy)
+        : "memory");
 }
-
-// Build-time tuning knob: how many W boxes ahead of the shared-memory ring
-// the producer prefetches into L2 (0 = no prefetch).
-#ifndef TINYM_L2_PREFETCH_BOXES
-#define TINYM_L2_PREFETCH_BOXES 0
-#endif
 
 // L2 eviction policies for the streamed weight (read once) and the
 // activation (re-read by every CTA).

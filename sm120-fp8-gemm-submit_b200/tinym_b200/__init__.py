@@ -169,10 +169,11 @@ def check_plan(m: int, n: int, k: int, plan: Plan) -> Plan:
 
 
 def make_plan(kernel: int = KERNEL_TC, split_k: int = 1, stages: int = 4, mma_n: int = 16,
-              consumer_warps: int = 0) -> Plan:
+              consumer_warps: int = 0, block_k: int = 128) -> Plan:
+    """An explicit plan (derived fields are filled by check_plan / the launch)."""
     p = Plan()
     p.kernel, p.split_k, p.stages, p.mma_n = kernel, split_k, stages, mma_n
-    p.consumer_warps, p.block_k = consumer_warps, 128
+    p.consumer_warps, p.block_k = consumer_warps, block_k
     return p
 
 

@@ -112,11 +112,21 @@ def test_check_plan_rejects_bad_plans():
         (1, t.make_plan(t.KERNEL_TC, 1, 4, 12)),            # MMA N not 8/16
         (1, t.make_plan(7, 1, 4, 8)),                       # unknown kernel
         (1, t.make_plan(t.KERNEL_TC, 8, 4, 8)),             # 8 splits of 7 K blocks
+        (1, t.make_plan(t.KERNEL_SIMT_M1, 1, 4, 0, 4, 256)),  # SIMT stages are 128 B of K
+        (9, t.make_plan(t.KERNEL_TC, 1, 4, 16, 0, 384)),      # block_k not 128/256/512
     ]
     for m, plan in bad:
         with pytest.raises(t.TinymError) as ei:
             t.check_plan(m, 1024, 896, plan)
         assert ei.value.status == 7, (m, plan.as_dict())
+
+
+def test_block_k_needs_whole_chunks():
+    import tinym_b200 as t
+
+    t.check_plan(9, 512, 1024, t.make_plan(t.KERNEL_TC, 1, 2, 16, 0, 512))
+    with pytest.raises(t.TinymError):
+        t.check_plan(9, 512, 1040, t.make_plan(t.KERNEL_TC, 1, 4, 16, 0, 256))
 
 
 def test_argument_checks_before_any_cuda_call():

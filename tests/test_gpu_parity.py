@@ -140,6 +140,14 @@ def test_ragged_shapes(cuda_device, oracle, m, k, n):
     _check(oracle, out, xq, wq, alpha)
 
 
+def _valid(tinym_b200, m, k, n, plan):
+    try:
+        tinym_b200.check_plan(m, n, k, plan)
+        return True
+    except tinym_b200.TinymError:
+        return False
+
+
 def _plans_for(tinym_b200, m, k, n):
     plans = []
     kb = (k + 127) // 128
@@ -149,7 +157,9 @@ def _plans_for(tinym_b200, m, k, n):
             continue
         for stages in (2, 4, 7):
             for mma_n in ((8, 16) if m <= 8 else (16,)):
-                plans.append(tinym_b200.make_plan(tinym_b200.KERNEL_TC, split, stages, mma_n))
+                for bk in ((128, 256, 512) if k % 128 == 0 else (128,)):
+                    plans.append(tinym_b200.make_plan(tinym_b200.KERNEL_TC, split, stages, mma_n,
+                                                      block_k=bk))
             if m == 1:
                 for cw in (4, 8):
                     plans.append(tinym_b200.make_plan(tinym_b200.KERNEL_SIMT_M1, split, stages,
@@ -157,7 +167,7 @@ def _plans_for(tinym_b200, m, k, n):
     return plans
 
 
-@pytest.mark.parametrize("m,k,n", [(1, 1024, 384), (7, 1152, 256), (16, 896, 300)])
+@pytest.mark.parametrize("m,k,n", [(1, 1024, 384), (7, 1152, 256), (16, 896, 300), (9, 1040, 200)])
 def test_explicit_plans(cuda_device, oracle, m, k, n):
     """Every kernel family, split-K cluster size, ring depth and MMA N."""
     import torch
@@ -190,7 +200,9 @@ def test_simt_m1_and_splits_full_size(cuda_device, oracle, m, k, n):
     xq, wq, sx, sw, alpha = oracle.make_case(m, k, n, seed=5, dist="normal")
     x, w = _to_dev(xq, cuda_device), _to_dev(wq, cuda_device)
     a = torch.from_numpy(alpha).to(cuda_device)
-    plans = [tinym_b200.make_plan(tinym_b200.KERNEL_TC, s, 6, 16) for s in (1, 2, 4, 8)]
+    plans = [tinym_b200.make_plan(tinym_b200.KERNEL_TC, s, st, 16, block_k=bk)
+             for s in (1, 2, 4, 8) for (st, bk) in ((6, 128), (5, 256), (3, 512))]
+    plans = [p for p in plans if _valid(tinym_b200, m, k, n, p)]
     if m == 1:
         plans += [tinym_b200.make_plan(tinym_b200.KERNEL_SIMT_M1, s, 6, 0, cw)
                   for s in (1, 3) for cw in (4, 8)]

@@ -40,10 +40,13 @@ constexpr int kMaxDevices = 64;
 constexpr int kMaxSplit = 8;       // portable cluster size
 constexpr int kMaxStages = 12;
 constexpr int kSmemLimit = 232448; // 227 KiB opt-in per CTA on sm_100
-// Per-CTA budget for two resident CTAs per SM: 228 KiB per SM, less 1 KiB
-// reserved per CTA, halved.
-constexpr uint32_t kSmemTwoPerSm = (233472u - 2u * 1024u) / 2u;
 constexpr uint64_t kDefaultTimeoutNs = 1000000000ull;  // 1 s per wait
+
+// Build-time knob: launch with programmatic dependent launch (1, default).
+#ifndef TINYM_USE_PDL
+#define TINYM_USE_PDL 1
+#endif
+constexpr bool kUsePdl = TINYM_USE_PDL != 0;
 
 // Build-time tuning knob: L2 sector promotion of the TMA tensor maps.
 #ifndef TINYM_L2_PROMOTION
@@ -363,7 +366,11 @@ int kernel_for(const tinym_plan& p, DeviceInfo* di, const void** fn) {
     return TINYM_OK;
 }
 
-// Grid (split_k x tiles_n), block, shared memory and cluster attribute.
+// Grid (split_k x tiles_n), block, shared memory, cluster attribute and
+// programmatic dependent launch.  `attrs` must hold 2 entries.  With PDL
+// the kernel may be scheduled while the previous kernel in the stream is
+// finishing; it runs its prologue and then blocks in griddepcontrol.wait
+// before touching global memory, so stream semantics are unchanged.
 void launch_config(const tinym_plan& p, void* stream, cudaLaunchConfig_t* cfg,
                    cudaLaunchAttribute* attrs) {
     *cfg = cudaLaunchConfig_t{};
@@ -371,15 +378,19 @@ void launch_config(const tinym_plan& p, void* stream, cudaLaunchConfig_t* cfg,
     cfg->blockDim = dim3(static_cast<unsigned>(p.threads), 1, 1);
     cfg->dynamicSmemBytes = static_cast<size_t>(p.smem_bytes);
     cfg->stream = static_cast<cudaStream_t>(stream);
-    cfg->numAttrs = 0;
+    unsigned n = 0;
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = kUsePdl ? 1 : 0;
+    ++n;
     if (p.split_k > 1) {
-        attrs[0].id = cudaLaunchAttributeClusterDimension;
-        attrs[0].val.clusterDim.x = static_cast<unsigned>(p.split_k);
-        attrs[0].val.clusterDim.y = 1;
-        attrs[0].val.clusterDim.z = 1;
-        cfg->attrs = attrs;
-        cfg->numAttrs = 1;
+        attrs[n].id = cudaLaunchAttributeClusterDimension;
+        attrs[n].val.clusterDim.x = static_cast<unsigned>(p.split_k);
+        attrs[n].val.clusterDim.y = 1;
+        attrs[n].val.clusterDim.z = 1;
+        ++n;
     }
+    cfg->attrs = attrs;
+    cfg->numAttrs = n;
 }
 
 // How many clusters of this plan can be resident at once (cached).
@@ -407,7 +418,7 @@ int max_active_clusters(const tinym_plan& p, int dev, DeviceInfo* di, int* out) 
         }
     }
     cudaLaunchConfig_t cfg;
-    cudaLaunchAttribute attrs[1];
+    cudaLaunchAttribute attrs[2];
     launch_config(p, nullptr, &cfg, attrs);
     int n = 0;
     if (p.split_k > 1) {
@@ -538,7 +549,7 @@ static int gemm_impl(const void* x, const void* w, void* y, int64_t ldy, int64_t
     const void* fn = nullptr;
     if ((st = kernel_for(p, di, &fn)) != TINYM_OK) return st;
     cudaLaunchConfig_t cfg{};
-    cudaLaunchAttribute attrs[1];
+    cudaLaunchAttribute attrs[2];
     launch_config(p, stream, &cfg, attrs);
     void* args[3] = {&tm_w, &tm_x, &prm};
     e = cudaLaunchKernelExC(&cfg, fn, args);

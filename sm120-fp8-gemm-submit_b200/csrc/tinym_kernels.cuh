@@ -219,10 +219,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         TINYM_TRACE(10);
         pol_w = l2_policy_w();
         pol_x = l2_policy_evict_last();
+        // Programmatic dependent launch: everything above overlaps the
+        // previous kernel's tail; no global memory is read before it has
+        // completed and its writes are visible.
+        grid_dependency_wait();
         for (; issued < min(stages, n_issue); ++issued) {
             issue(issued);
             if (issued == 0) TINYM_TRACE(11);
         }
+        // Let the next kernel in the stream start its own prologue on SMs
+        // as they free up (it still waits for this grid to complete).
+        grid_launch_dependents();
         TINYM_TRACE(1);
         // The cluster leader expects one partial-sum block from each other
         // CTA of its cluster (st.async, completing bytes on red_bar).
@@ -289,7 +296,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
     } else {
         // ---------------- epilogue warps 2..5: TMEM lanes 32*(warp%4) ..
-        alpha = load_alpha(p);  // issued early: its latency hides behind the mainloop
+        grid_dependency_wait();  // alpha may be written by the previous kernel
+        alpha = load_alpha(p);   // issued early: its latency hides behind the mainloop
         // tcgen05.ld is .sync.aligned: the whole warp takes the same branch.
         const bool ready = mbar_wait(acc_bar, 0, guard, kErrEpilogueWait) && !*abort_flag;
         if (__all_sync(0xFFFFFFFFu, ready)) {
@@ -449,7 +457,9 @@ __global__ void __launch_bounds__(32 * (CWARPS + 1), 1)
         fence_proxy_async_smem();
         pol_w = l2_policy_w();
         pol_x = l2_policy_evict_last();
+        grid_dependency_wait();
         for (; issued < min(stages, n_issue); ++issued) issue(issued);  // first ring-full
+        grid_launch_dependents();
     }
     __syncthreads();
     if (p.split > 1) cluster_arrive_relaxed();
@@ -537,6 +547,7 @@ __global__ void __launch_bounds__(32 * (CWARPS + 1), 1)
     const bool writer = have_acc && chunk == 0;
     if (p.split == 1) {
         if (writer) {
+            grid_dependency_wait();
             const float alpha = load_alpha(p);
 #pragma unroll
             for (int pp = 0; pp < kPasses; ++pp) {
@@ -558,6 +569,7 @@ __global__ void __launch_bounds__(32 * (CWARPS + 1), 1)
         cluster_arrive_release();
         cluster_wait_acquire();
         if (writer && split_idx == 0) {
+            grid_dependency_wait();
             const float alpha = load_alpha(p);
 #pragma unroll
             for (int pp = 0; pp < kPasses; ++pp) {

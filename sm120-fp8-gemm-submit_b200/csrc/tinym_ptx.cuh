@@ -35,6 +35,18 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
     return r;
 }
 
+// ---------------------------------------------------------------- dependent launch
+// Block until the grids this one depends on (programmatic stream
+// serialisation) have completed and their memory is visible; a no-op when
+// the kernel was launched without the attribute.
+__device__ __forceinline__ void grid_dependency_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+// Allow the next dependent grid in the stream to be scheduled.
+__device__ __forceinline__ void grid_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");

@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define TINYM_ABI_VERSION 1
+#define TINYM_ABI_VERSION 2
 
 /* Exported-symbol marker (the library is built with hidden visibility). */
 #if defined(__GNUC__)
@@ -70,12 +70,13 @@ typedef enum tinym_status {
  * accepted back by tinym_fp8_gemm_ex for sweeps. */
 typedef struct tinym_plan {
     int32_t kernel;         /* TINYM_KERNEL_* */
-    int32_t split_k;        /* CTAs per 128-row W tile (K split, 1..8); >1 => cluster of split_k CTAs */
+    int32_t split_k;        /* CTAs per W tile (K split, 1..8); >1 => cluster of split_k CTAs */
     int32_t stages;         /* shared-memory ring depth (W+X stages) */
     int32_t mma_n;          /* TC: MMA N (8 or 16, >= M); SIMT: 0 */
     int32_t consumer_warps; /* SIMT: dequant/FMA warps (4 or 8); TC: 0 */
-    int32_t block_k;        /* K bytes per stage (128) */
-    int32_t tiles_n;        /* out: ceil(N / 128) */
+    int32_t block_k;        /* K bytes per stage: 128, or 256 / 512 (TC, K % 128 == 0); 0 = 128 */
+    int32_t tile_m;         /* W rows per CTA tile (= MMA M): 128, or 64 (TC); 0 = 128 */
+    int32_t tiles_n;        /* out: ceil(N / tile_m) */
     int32_t grid_ctas;      /* out: CTAs launched = tiles_n * split_k */
     int32_t smem_bytes;     /* out: dynamic shared memory per CTA */
     int32_t threads;        /* out: threads per CTA */

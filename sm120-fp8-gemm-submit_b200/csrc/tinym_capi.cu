@@ -203,7 +203,7 @@ int get_map(const void* ptr, int64_t rows, int64_t cols, int box_rows, int swizz
 // ---------------------------------------------------------------- plans
 int plan_chunks(const tinym_plan& p) { return p.block_k / kBlockK; }
 
-int w_stage_bytes(const tinym_plan& p) { return plan_chunks(p) * tinym::kWStageBytes; }
+int w_stage_bytes(const tinym_plan& p) { return plan_chunks(p) * p.tile_m * kBlockK; }
 
 int x_stage_bytes(const tinym_plan& p) {
     return p.kernel == TINYM_KERNEL_TC ? plan_chunks(p) * p.mma_n * kBlockK : kBlockK;
@@ -220,9 +220,13 @@ uint32_t plan_smem_bytes(const tinym_plan& p) {
 }
 
 int fill_derived(int64_t m, int64_t n, int64_t k, tinym_plan* p) {
-    const int64_t tiles = (n + kTileRows - 1) / kTileRows;
+    if (p->block_k == 0) p->block_k = kBlockK;  // 0 selects the defaults
+    if (p->tile_m == 0) p->tile_m = kTileRows;
     if (p->kernel != TINYM_KERNEL_TC && p->kernel != TINYM_KERNEL_SIMT_M1)
         return fail(TINYM_ERR_BAD_PLAN, "plan.kernel %d is not a kernel family", p->kernel);
+    if (p->tile_m != 128 && !(p->tile_m == 64 && p->kernel == TINYM_KERNEL_TC))
+        return fail(TINYM_ERR_BAD_PLAN, "plan.tile_m must be 128, or 64 for the TC kernel");
+    const int64_t tiles = (n + p->tile_m - 1) / p->tile_m;
     if (p->block_k != 128 && p->block_k != 256 && p->block_k != 512)
         return fail(TINYM_ERR_BAD_PLAN, "plan.block_k must be 128, 256 or 512");
     if (p->block_k != kBlockK && (p->kernel != TINYM_KERNEL_TC || k % kBlockK != 0))
@@ -256,11 +260,13 @@ int fill_derived(int64_t m, int64_t n, int64_t k, tinym_plan* p) {
     if (smem > static_cast<uint32_t>(kSmemLimit))
         return fail(TINYM_ERR_BAD_PLAN, "plan needs %u bytes of shared memory (> %d)", smem,
                     kSmemLimit);
-    if (p->kernel == TINYM_KERNEL_TC &&
-        (p->split_k - 1) * tinym::tc_red_rank_bytes(p->mma_n) > p->stages * w_stage_bytes(*p))
+    const int red = p->kernel == TINYM_KERNEL_TC
+                        ? (p->split_k - 1) * tinym::tc_red_rank_bytes(p->mma_n, p->tile_m)
+                        : 0;
+    if (red > p->stages * w_stage_bytes(*p))
         return fail(TINYM_ERR_BAD_PLAN,
                     "split_k %d needs %d bytes of partial sums, more than the %d-stage ring holds",
-                    p->split_k, (p->split_k - 1) * tinym::tc_red_rank_bytes(p->mma_n), p->stages);
+                    p->split_k, red, p->stages);
     p->tiles_n = static_cast<int32_t>(tiles);
     p->grid_ctas = static_cast<int32_t>(tiles * p->split_k);
     p->smem_bytes = static_cast<int32_t>(smem);
@@ -286,8 +292,9 @@ int check_shape(int64_t m, int64_t n, int64_t k) {
 // Ring depth for a TC plan: enough stages to cover the CTA's K blocks (no
 // more is useful) and to hold the split-K partials the leader receives in
 // its ring, at most max_st; -1 if the partials cannot fit.
-int tc_stages_for(int split, int64_t kb_per_cta, int mma_n, int w_stage, int max_st) {
-    const int red = (split - 1) * tinym::tc_red_rank_bytes(mma_n);
+int tc_stages_for(int split, int64_t kb_per_cta, int mma_n, int tile_m, int w_stage,
+                  int max_st) {
+    const int red = (split - 1) * tinym::tc_red_rank_bytes(mma_n, tile_m);
     const int need_red = (red + w_stage - 1) / w_stage;
     const int64_t st = std::max<int64_t>({2, kb_per_cta < max_st ? kb_per_cta : max_st, need_red});
     return st > max_st ? -1 : static_cast<int>(st);
@@ -305,54 +312,60 @@ int max_stages_fitting(const tinym_plan& p, uint32_t limit) {
     return st;
 }
 
-// Heuristic part of the dispatch table, fitted to B200 measurements of all
-// six official points (plan sweeps: one CTA per SM with a deep ring beat
-// two CTAs per SM everywhere; a CTA's TMA stream is bound by instructions,
-// so the widest stage wins):
-//  * block_k = 512 (one 64 KiB W box per TMA instruction) whenever
-//    K % 128 == 0, else 128 (2-D boxes; TMA zero-fills the K tail);
-//  * as many stages as fit 227 KiB;
+// Heuristic part of the dispatch table, fitted to B200 measurements of the
+// official points (plan sweeps, per-CTA %globaltimer traces):
+//  * one CTA per SM with a deep ring (two CTAs per SM never won);
+//  * block_k = 512 -- one 64 KiB 3-D TMA box of W per stage -- whenever
+//    K % 128 == 0 (a CTA's TMA stream is instruction-bound), else 128;
+//  * 128-row W tiles (64-row tiles need no K split on N = 5120 / 8192 but
+//    stream only ~37 GB/s per CTA with 32 KiB boxes, which loses);
 //  * the largest K split (cluster size <= 8) that keeps tiles * split CTAs
-//    within one CTA per SM and gives every CTA >= 2 stages.
-tinym_plan heuristic_plan(int64_t m, int64_t k, int64_t tiles, int sm_count) {
+//    within one CTA per SM and gives every CTA >= 2 stages;
+//  * as many stages as fit 227 KiB.
+tinym_plan heuristic_plan(int64_t m, int64_t n, int64_t k, int sm_count) {
     tinym_plan p{};
     p.kernel = TINYM_KERNEL_TC;
     p.mma_n = m <= 8 ? 8 : 16;
     p.block_k = (k % kBlockK == 0) ? 4 * kBlockK : kBlockK;
     p.split_k = 1;
+    p.tile_m = kTileRows;
+    const int64_t tiles = (n + p.tile_m - 1) / p.tile_m;
     const int64_t kb = (k + p.block_k - 1) / p.block_k;
     const int max_st = max_stages_fitting(p, static_cast<uint32_t>(kSmemLimit));
     for (int s = 2; s <= kMaxSplit; ++s) {
         if (tiles * s > sm_count) break;
         const int64_t per = (kb + s - 1) / s;
         if (per < 2 || (s - 1) * per >= kb) continue;
-        if (tc_stages_for(s, per, p.mma_n, w_stage_bytes(p), max_st) < 0) continue;
+        if (tc_stages_for(s, per, p.mma_n, p.tile_m, w_stage_bytes(p), max_st) < 0) continue;
         p.split_k = s;
     }
-    p.stages = tc_stages_for(p.split_k, (kb + p.split_k - 1) / p.split_k, p.mma_n,
+    p.stages = tc_stages_for(p.split_k, (kb + p.split_k - 1) / p.split_k, p.mma_n, p.tile_m,
                              w_stage_bytes(p), max_st);
     return p;
 }
 
 // Kernel entry for a plan; sets the shared-memory opt-in once per device.
 int kernel_for(const tinym_plan& p, DeviceInfo* di, const void** fn) {
-    static const void* const kTc[2][3] = {
-        {reinterpret_cast<const void*>(&tinym::tinym_tc_kernel<8, 1>),
-         reinterpret_cast<const void*>(&tinym::tinym_tc_kernel<8, 2>),
-         reinterpret_cast<const void*>(&tinym::tinym_tc_kernel<8, 4>)},
-        {reinterpret_cast<const void*>(&tinym::tinym_tc_kernel<16, 1>),
-         reinterpret_cast<const void*>(&tinym::tinym_tc_kernel<16, 2>),
-         reinterpret_cast<const void*>(&tinym::tinym_tc_kernel<16, 4>)}};
+#define TINYM_TC(N, C, T) reinterpret_cast<const void*>(&tinym::tinym_tc_kernel<N, C, T>)
+    static const void* const kTc[2][3][2] = {
+        {{TINYM_TC(8, 1, 64), TINYM_TC(8, 1, 128)},
+         {TINYM_TC(8, 2, 64), TINYM_TC(8, 2, 128)},
+         {TINYM_TC(8, 4, 64), TINYM_TC(8, 4, 128)}},
+        {{TINYM_TC(16, 1, 64), TINYM_TC(16, 1, 128)},
+         {TINYM_TC(16, 2, 64), TINYM_TC(16, 2, 128)},
+         {TINYM_TC(16, 4, 64), TINYM_TC(16, 4, 128)}}};
+#undef TINYM_TC
     uint32_t attr_bit = 0;
     if (p.kernel == TINYM_KERNEL_TC) {
         const int ni = p.mma_n == 8 ? 0 : 1;
         const int ci = p.block_k == 128 ? 0 : (p.block_k == 256 ? 1 : 2);
-        *fn = kTc[ni][ci];
-        attr_bit = 1u << (ni * 3 + ci);
+        const int ti = p.tile_m == 64 ? 0 : 1;
+        *fn = kTc[ni][ci][ti];
+        attr_bit = 1u << ((ni * 3 + ci) * 2 + ti);
     } else {
         *fn = p.consumer_warps == 4 ? reinterpret_cast<const void*>(&tinym::tinym_simt_m1_kernel<4>)
                                     : reinterpret_cast<const void*>(&tinym::tinym_simt_m1_kernel<8>);
-        attr_bit = p.consumer_warps == 4 ? 1u << 6 : 1u << 7;
+        attr_bit = p.consumer_warps == 4 ? 1u << 12 : 1u << 13;
     }
     if (!(di->attr_done.load(std::memory_order_acquire) & attr_bit)) {
         cudaError_t e = cudaFuncSetAttribute(*fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
@@ -475,8 +488,7 @@ int tinym_select_plan(int64_t m, int64_t n, int64_t k, int32_t sm_count, tinym_p
     if (sm_count < 1) return fail(TINYM_ERR_INVALID_ARGUMENT, "sm_count must be positive");
     int st = check_shape(m, n, k);
     if (st != TINYM_OK) return st;
-    const int64_t tiles = (n + kTileRows - 1) / kTileRows;
-    *out = heuristic_plan(m, k, tiles, sm_count);
+    *out = heuristic_plan(m, n, k, sm_count);
     return fill_derived(m, n, k, out);
 }
 
@@ -516,7 +528,7 @@ static int gemm_impl(const void* x, const void* w, void* y, int64_t ldy, int64_t
             const int64_t kb = (k + p.block_k - 1) / p.block_k;
             const int max_st = max_stages_fitting(p, static_cast<uint32_t>(kSmemLimit));
             const int s2 = tc_stages_for(p.split_k, (kb + p.split_k - 1) / p.split_k, p.mma_n,
-                                         w_stage_bytes(p), max_st);
+                                         p.tile_m, w_stage_bytes(p), max_st);
             if (s2 > 0) p.stages = std::max(p.stages, s2);
             if ((st = fill_derived(m, n, k, &p)) != TINYM_OK) return st;
         }
@@ -524,7 +536,7 @@ static int gemm_impl(const void* x, const void* w, void* y, int64_t ldy, int64_t
 
     CUtensorMap tm_w, tm_x;
     const int chunks = plan_chunks(p);
-    if ((st = get_map(w, n, k, kTileRows, 1, chunks, dev, &tm_w)) != TINYM_OK) return st;
+    if ((st = get_map(w, n, k, p.tile_m, 1, chunks, dev, &tm_w)) != TINYM_OK) return st;
     if (p.kernel == TINYM_KERNEL_TC) {
         if ((st = get_map(x, m, k, p.mma_n, 1, chunks, dev, &tm_x)) != TINYM_OK) return st;
     } else {

@@ -59,7 +59,7 @@ enum : uint32_t {
     kErrReduceWait = 1u << 5,
 };
 
-constexpr int kTileRows = 128;   // W rows per tile (= MMA M)
+constexpr int kTileRows = 128;   // W rows per tile of the SIMT kernel (and the TC default)
 constexpr int kBlockK = 128;     // K bytes of one chunk (= one 128B swizzle row)
 constexpr int kWStageBytes = kTileRows * kBlockK;  // one W chunk: 16 KiB
 constexpr int kTcThreads = 192;  // warp0 TMA, warp1 MMA, warps2-5 epilogue
@@ -115,8 +115,8 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 // non-leader CTAs send to their cluster leader: MMA_N values padded by 4 so
 // that the leader's 16-byte shared-memory reads are bank-conflict free.
 __host__ __device__ constexpr int tc_red_stride(int mma_n) { return mma_n + 4; }
-__host__ __device__ constexpr int tc_red_rank_bytes(int mma_n) {
-    return kTileRows * tc_red_stride(mma_n) * 4;
+__host__ __device__ constexpr int tc_red_rank_bytes(int mma_n, int tile_m) {
+    return tile_m * tc_red_stride(mma_n) * 4;
 }
 
 // Named barrier 1 over the 128 epilogue threads (warps 2..5) of the TC kernel.
@@ -131,25 +131,31 @@ __device__ __forceinline__ float load_alpha(const TinymParams& p) {
 // =====================================================================
 // tcgen05 swap-AB kernel
 // =====================================================================
-template <int MMA_N, int CHUNKS>
+template <int MMA_N, int CHUNKS, int TILE_M>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tinym_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
                     const __grid_constant__ CUtensorMap tm_x, const TinymParams p) {
     static_assert(MMA_N == 8 || MMA_N == 16, "MMA_N must be 8 or 16");
     static_assert(CHUNKS == 1 || CHUNKS == 2 || CHUNKS == 4, "1, 2 or 4 K chunks per stage");
+    static_assert(TILE_M == 64 || TILE_M == 128, "W tiles of 64 or 128 rows (MMA M)");
     // One stage = CHUNKS K chunks of 128 bytes.  Each W chunk is a standard
-    // [128 rows x 128 B] 128B-swizzled tile (16 KiB), each X chunk
+    // [TILE_M rows x 128 B] 128B-swizzled tile, each X chunk
     // [MMA_N rows x 128 B]; with CHUNKS > 1 one 3-D TMA box fetches all of
     // a stage's chunks, which raises the bytes moved per TMA instruction
     // (a single CTA's stream is bound by instructions, not bytes).
+    // TILE_M = 64 halves the tile so that more CTAs cover N without a K
+    // split; its M=64 accumulator occupies TMEM lanes 32q..32q+15 (rows
+    // 16q..16q+15) of each 32-lane subpartition q.
+    constexpr int kWChunk = TILE_M * kBlockK;
     constexpr int kXChunkBytes = MMA_N * kBlockK;  // 1 or 2 KiB, 1024-aligned
-    constexpr int kWStage = CHUNKS * kWStageBytes;
+    constexpr int kWStage = CHUNKS * kWChunk;
     constexpr int kXStageBytes = CHUNKS * kXChunkBytes;
     constexpr uint32_t kStageTx = kWStage + kXStageBytes;
-    constexpr uint32_t kIdesc = idesc_e4m3_f32(kTileRows, MMA_N);
+    constexpr uint32_t kIdesc = idesc_e4m3_f32(TILE_M, MMA_N);
     constexpr int kRedStride = tc_red_stride(MMA_N);
-    constexpr int kRedRankBytes = kTileRows * kRedStride * 4;  // per-rank block in the ring
-    constexpr int kRedSendBytes = kTileRows * MMA_N * 4;       // bytes a rank actually sends
+    constexpr int kRedRankBytes = TILE_M * kRedStride * 4;  // per-rank block in the ring
+    constexpr int kRedSendBytes = TILE_M * MMA_N * 4;       // bytes a rank actually sends
+    constexpr int kRowsPerWarp = TILE_M / 4;                // accumulator rows per epilogue warp
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
@@ -195,11 +201,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int chunk = (kb0 + i) * CHUNKS;  // first 128-byte K chunk of the stage
         mbar_expect_tx(full_bar(s), kStageTx);
         if constexpr (CHUNKS == 1) {
-            tma_load_2d(w_ring + s * kWStage, &tm_w, full_bar(s), chunk * kBlockK, tile * kTileRows,
+            tma_load_2d(w_ring + s * kWStage, &tm_w, full_bar(s), chunk * kBlockK, tile * TILE_M,
                         pol_w);
             tma_load_2d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), chunk * kBlockK, 0, pol_x);
         } else {
-            tma_load_3d(w_ring + s * kWStage, &tm_w, full_bar(s), 0, tile * kTileRows, chunk, pol_w);
+            tma_load_3d(w_ring + s * kWStage, &tm_w, full_bar(s), 0, tile * TILE_M, chunk, pol_w);
             tma_load_3d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), 0, 0, chunk, pol_x);
         }
     };
@@ -280,7 +286,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tc_fence_after_sync();
 #pragma unroll
                 for (int c = 0; c < CHUNKS; ++c) {
-                    const uint32_t a0 = w_ring + s * kWStage + c * kWStageBytes;
+                    const uint32_t a0 = w_ring + s * kWStage + c * kWChunk;
                     const uint32_t b0 = x_ring + s * kXStageBytes + c * kXChunkBytes;
 #pragma unroll
                     for (int kk = 0; kk < kBlockK / 32; ++kk) {
@@ -315,13 +321,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncwarp();
 
     // ---------------- split-K reduction through distributed shared memory
-    const int row = (warp & 3) * 32 + lane;  // W row within the tile (epilogue warps)
+    // Epilogue thread (warp w, lane t) holds TMEM lane 32*(w%4)+t, which is
+    // tile row (w%4)*kRowsPerWarp + t for t < kRowsPerWarp.
+    const int row = (warp & 3) * kRowsPerWarp + lane;
     const bool epi = warp >= 2;
+    const bool row_ok = epi && lane < kRowsPerWarp;
     if (clustered) {
         if (leader) cluster_arrive_release();  // leader's MMAs retired: ring is free
         cluster_wait_acquire();
         if (threadIdx.x == 64) TINYM_TRACE(6);
-        if (epi && !leader) {
+        if (row_ok && !leader) {
             // Push this CTA's partial row block into the leader's ring,
             // [rank-1][row][kRedStride].  Every epilogue thread always sends
             // (zeros if it has no accumulator) so the leader's wait ends.
@@ -336,7 +345,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int j = 0; j < 4; ++j) v[j] = have_acc ? acc[c + j] : 0.f;
                 st_async_v4(dst + 16u * (c / 4), v, rbar);
             }
-        } else if (epi) {
+        } else if (row_ok) {
             // Leader: wait for every other rank's partials (bounded), then
             // fold them into the accumulator in K order (rank 0 first), so
             // the result does not depend on arrival order.
@@ -365,19 +374,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ---------------- output: BF16 tile staged in shared memory, then
     // written row by row with 16-byte stores (8 consecutive N per store).
     if (epi && (!clustered || leader)) {
-        if (have_acc) {
+        if (have_acc && row_ok) {
 #pragma unroll
             for (int m = 0; m < MMA_N; ++m)
-                ystage[m * kTileRows + row] = __float2bfloat16_rn(acc[m] * alpha);
+                ystage[m * TILE_M + row] = __float2bfloat16_rn(acc[m] * alpha);
         }
         epilogue_bar_sync();  // the 4 epilogue warps only
         if (!*abort_flag) {
-            const int n0 = tile * kTileRows;
+            const int n0 = tile * TILE_M;
             const bool vec = ((reinterpret_cast<uintptr_t>(p.y) & 15u) == 0) && (p.ldy % 8 == 0);
-            for (int c = row; c < p.m * (kTileRows / 8); c += kTileRows) {
-                const int m = c / (kTileRows / 8);
-                const int j = (c % (kTileRows / 8)) * 8;
-                const __nv_bfloat16* src = ystage + m * kTileRows + j;
+            for (int c = threadIdx.x - 64; c < p.m * (TILE_M / 8); c += 128) {
+                const int m = c / (TILE_M / 8);
+                const int j = (c % (TILE_M / 8)) * 8;
+                const __nv_bfloat16* src = ystage + m * TILE_M + j;
                 __nv_bfloat16* dst = p.y + static_cast<size_t>(m) * p.ldy + n0 + j;
                 if (vec && n0 + j + 8 <= p.n) {
                     *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);

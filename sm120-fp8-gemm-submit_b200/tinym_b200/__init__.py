@@ -67,6 +67,7 @@ class Plan(ctypes.Structure):
         ("mma_n", ctypes.c_int32),
         ("consumer_warps", ctypes.c_int32),
         ("block_k", ctypes.c_int32),
+        ("tile_m", ctypes.c_int32),
         ("tiles_n", ctypes.c_int32),
         ("grid_ctas", ctypes.c_int32),
         ("smem_bytes", ctypes.c_int32),
@@ -169,11 +170,11 @@ def check_plan(m: int, n: int, k: int, plan: Plan) -> Plan:
 
 
 def make_plan(kernel: int = KERNEL_TC, split_k: int = 1, stages: int = 4, mma_n: int = 16,
-              consumer_warps: int = 0, block_k: int = 128) -> Plan:
+              consumer_warps: int = 0, block_k: int = 128, tile_m: int = 128) -> Plan:
     """An explicit plan (derived fields are filled by check_plan / the launch)."""
     p = Plan()
     p.kernel, p.split_k, p.stages, p.mma_n = kernel, split_k, stages, mma_n
-    p.consumer_warps, p.block_k = consumer_warps, block_k
+    p.consumer_warps, p.block_k, p.tile_m = consumer_warps, block_k, tile_m
     return p
 
 

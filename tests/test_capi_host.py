@@ -33,7 +33,7 @@ def test_library_exports_every_declared_symbol():
     lib = tinym_b200.capi()
     for name in declared_symbols():
         assert hasattr(lib, name), name
-    assert lib.tinym_abi_version() == 1
+    assert lib.tinym_abi_version() == 2
 
 
 def test_status_strings():
@@ -48,7 +48,7 @@ def test_status_strings():
 def test_plan_struct_layout():
     import tinym_b200
 
-    assert ctypes.sizeof(tinym_b200.Plan) == 40
+    assert ctypes.sizeof(tinym_b200.Plan) == 44
 
 
 @pytest.mark.parametrize("m,k,n", OFFICIAL)
@@ -61,7 +61,7 @@ def test_dispatch_table_official_points(m, k, n):
     assert p.smem_bytes <= 232448
     per_sm = 2 if p.smem_bytes <= (233472 - 2048) // 2 else 1
     assert p.grid_ctas <= per_sm * 148
-    assert p.tiles_n == (n + 127) // 128
+    assert p.tiles_n == (n + p.tile_m - 1) // p.tile_m
     kb = (k + 127) // 128
     per = -(-kb // p.split_k)
     assert (p.split_k - 1) * per < kb  # no empty K range
@@ -114,11 +114,33 @@ def test_check_plan_rejects_bad_plans():
         (1, t.make_plan(t.KERNEL_TC, 8, 4, 8)),             # 8 splits of 7 K blocks
         (1, t.make_plan(t.KERNEL_SIMT_M1, 1, 4, 0, 4, 256)),  # SIMT stages are 128 B of K
         (9, t.make_plan(t.KERNEL_TC, 1, 4, 16, 0, 384)),      # block_k not 128/256/512
+        (1, t.make_plan(t.KERNEL_SIMT_M1, 1, 4, 0, 4, 128, 64)),  # SIMT tiles are 128 rows
+        (9, t.make_plan(t.KERNEL_TC, 1, 4, 16, 0, 128, 32)),  # tile_m not 64/128
     ]
     for m, plan in bad:
         with pytest.raises(t.TinymError) as ei:
             t.check_plan(m, 1024, 896, plan)
         assert ei.value.status == 7, (m, plan.as_dict())
+
+
+def test_zero_plan_fields_mean_defaults():
+    import tinym_b200 as t
+
+    p = t.make_plan(t.KERNEL_TC, 1, 4, 16, 0, 0, 0)
+    q = t.check_plan(9, 512, 1024, p)
+    assert q.block_k == 128 and q.tile_m == 128 and q.tiles_n == 4
+
+
+def test_dispatch_tiles_for_official_points():
+    """The measured winners on B200: 128-row tiles, 64 KiB stages, K split
+    3 / 2 / 1 for N = 5120 / 8192 / 16384."""
+    import tinym_b200 as t
+
+    for m in (1, 9, 16):
+        for k, n, tile, split in ((6144, 5120, 128, 3), (5120, 8192, 128, 2),
+                                  (5120, 16384, 128, 1)):
+            p = t.select_plan(m, n, k, 148)
+            assert (p.tile_m, p.split_k, p.block_k) == (tile, split, 512), p.as_dict()
 
 
 def test_block_k_needs_whole_chunks():

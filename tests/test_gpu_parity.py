@@ -158,8 +158,9 @@ def _plans_for(tinym_b200, m, k, n):
         for stages in (2, 4, 7):
             for mma_n in ((8, 16) if m <= 8 else (16,)):
                 for bk in ((128, 256, 512) if k % 128 == 0 else (128,)):
-                    plans.append(tinym_b200.make_plan(tinym_b200.KERNEL_TC, split, stages, mma_n,
-                                                      block_k=bk))
+                    for tm in (64, 128):
+                        plans.append(tinym_b200.make_plan(tinym_b200.KERNEL_TC, split, stages,
+                                                          mma_n, block_k=bk, tile_m=tm))
             if m == 1:
                 for cw in (4, 8):
                     plans.append(tinym_b200.make_plan(tinym_b200.KERNEL_SIMT_M1, split, stages,
@@ -200,8 +201,9 @@ def test_simt_m1_and_splits_full_size(cuda_device, oracle, m, k, n):
     xq, wq, sx, sw, alpha = oracle.make_case(m, k, n, seed=5, dist="normal")
     x, w = _to_dev(xq, cuda_device), _to_dev(wq, cuda_device)
     a = torch.from_numpy(alpha).to(cuda_device)
-    plans = [tinym_b200.make_plan(tinym_b200.KERNEL_TC, s, st, 16, block_k=bk)
-             for s in (1, 2, 4, 8) for (st, bk) in ((6, 128), (5, 256), (3, 512))]
+    plans = [tinym_b200.make_plan(tinym_b200.KERNEL_TC, s, st, 16, block_k=bk, tile_m=tm)
+             for s in (1, 2, 4, 8) for (st, bk) in ((6, 128), (5, 256), (3, 512))
+             for tm in (64, 128)]
     plans = [p for p in plans if _valid(tinym_b200, m, k, n, p)]
     if m == 1:
         plans += [tinym_b200.make_plan(tinym_b200.KERNEL_SIMT_M1, s, 6, 0, cw)

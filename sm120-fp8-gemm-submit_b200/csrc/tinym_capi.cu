@@ -209,12 +209,14 @@ int x_stage_bytes(const tinym_plan& p) {
     return p.kernel == TINYM_KERNEL_TC ? plan_chunks(p) * p.mma_n * kBlockK : kBlockK;
 }
 
-// Dynamic shared memory of a plan.  The TC kernel receives split-K partials
-// in its W ring (no separate buffer); the SIMT kernel keeps a separate
-// (split - 1) x 128-float buffer.
+// Dynamic shared memory of a plan: the rings plus the split-K receive
+// blocks ((split - 1) x rows owned x padded MMA_N floats for the TC kernel,
+// (split - 1) x 128 floats for the SIMT kernel).
 uint32_t plan_smem_bytes(const tinym_plan& p) {
     if (p.kernel == TINYM_KERNEL_TC)
-        return tinym::smem_layout(p.stages, w_stage_bytes(p), x_stage_bytes(p), 1, 0).bytes;
+        return tinym::smem_layout(p.stages, w_stage_bytes(p), x_stage_bytes(p), p.split_k,
+                                  tinym::tc_red_rank_bytes(p.mma_n, p.tile_m, p.split_k))
+            .bytes;
     return tinym::smem_layout(p.stages, w_stage_bytes(p), x_stage_bytes(p), p.split_k,
                               kTileRows * 4).bytes;
 }
@@ -260,13 +262,6 @@ int fill_derived(int64_t m, int64_t n, int64_t k, tinym_plan* p) {
     if (smem > static_cast<uint32_t>(kSmemLimit))
         return fail(TINYM_ERR_BAD_PLAN, "plan needs %u bytes of shared memory (> %d)", smem,
                     kSmemLimit);
-    const int red = p->kernel == TINYM_KERNEL_TC
-                        ? (p->split_k - 1) * tinym::tc_red_rank_bytes(p->mma_n, p->tile_m)
-                        : 0;
-    if (red > p->stages * w_stage_bytes(*p))
-        return fail(TINYM_ERR_BAD_PLAN,
-                    "split_k %d needs %d bytes of partial sums, more than the %d-stage ring holds",
-                    p->split_k, red, p->stages);
     p->tiles_n = static_cast<int32_t>(tiles);
     p->grid_ctas = static_cast<int32_t>(tiles * p->split_k);
     p->smem_bytes = static_cast<int32_t>(smem);
@@ -289,27 +284,23 @@ int check_shape(int64_t m, int64_t n, int64_t k) {
     return TINYM_OK;
 }
 
-// Ring depth for a TC plan: enough stages to cover the CTA's K blocks (no
-// more is useful) and to hold the split-K partials the leader receives in
-// its ring, at most max_st; -1 if the partials cannot fit.
-int tc_stages_for(int split, int64_t kb_per_cta, int mma_n, int tile_m, int w_stage,
-                  int max_st) {
-    const int red = (split - 1) * tinym::tc_red_rank_bytes(mma_n, tile_m);
-    const int need_red = (red + w_stage - 1) / w_stage;
-    const int64_t st = std::max<int64_t>({2, kb_per_cta < max_st ? kb_per_cta : max_st, need_red});
-    return st > max_st ? -1 : static_cast<int>(st);
-}
-
-// Largest ring depth whose shared memory fits `limit` bytes.
+// Largest ring depth (>= 2) whose shared memory fits `limit` bytes, or -1
+// if not even two stages fit.
 int max_stages_fitting(const tinym_plan& p, uint32_t limit) {
-    int st = kMaxStages;
-    while (st > 2) {
+    for (int st = kMaxStages; st >= 2; --st) {
         tinym_plan q = p;
         q.stages = st;
-        if (plan_smem_bytes(q) <= limit) break;
-        --st;
+        if (plan_smem_bytes(q) <= limit) return st;
     }
-    return st;
+    return -1;
+}
+
+// Ring depth for a TC plan: as many stages as fit, but no more than the
+// CTA's K blocks (more is useless); -1 if not even two stages fit.
+int tc_stages_for(const tinym_plan& p, int64_t kb_per_cta) {
+    const int max_st = max_stages_fitting(p, static_cast<uint32_t>(kSmemLimit));
+    if (max_st < 0) return -1;
+    return static_cast<int>(std::max<int64_t>(2, std::min<int64_t>(kb_per_cta, max_st)));
 }
 
 // Heuristic part of the dispatch table, fitted to B200 measurements of the
@@ -331,16 +322,16 @@ tinym_plan heuristic_plan(int64_t m, int64_t n, int64_t k, int sm_count) {
     p.tile_m = kTileRows;
     const int64_t tiles = (n + p.tile_m - 1) / p.tile_m;
     const int64_t kb = (k + p.block_k - 1) / p.block_k;
-    const int max_st = max_stages_fitting(p, static_cast<uint32_t>(kSmemLimit));
     for (int s = 2; s <= kMaxSplit; ++s) {
         if (tiles * s > sm_count) break;
         const int64_t per = (kb + s - 1) / s;
         if (per < 2 || (s - 1) * per >= kb) continue;
-        if (tc_stages_for(s, per, p.mma_n, p.tile_m, w_stage_bytes(p), max_st) < 0) continue;
+        tinym_plan q = p;
+        q.split_k = s;
+        if (tc_stages_for(q, per) < 0) continue;
         p.split_k = s;
     }
-    p.stages = tc_stages_for(p.split_k, (kb + p.split_k - 1) / p.split_k, p.mma_n, p.tile_m,
-                             w_stage_bytes(p), max_st);
+    p.stages = tc_stages_for(p, (kb + p.split_k - 1) / p.split_k);
     return p;
 }
 
@@ -526,10 +517,10 @@ static int gemm_impl(const void* x, const void* w, void* y, int64_t ldy, int64_t
             if (clusters >= p.tiles_n) break;
             --p.split_k;
             const int64_t kb = (k + p.block_k - 1) / p.block_k;
-            const int max_st = max_stages_fitting(p, static_cast<uint32_t>(kSmemLimit));
-            const int s2 = tc_stages_for(p.split_k, (kb + p.split_k - 1) / p.split_k, p.mma_n,
-                                         p.tile_m, w_stage_bytes(p), max_st);
-            if (s2 > 0) p.stages = std::max(p.stages, s2);
+            const int s2 = p.kernel == TINYM_KERNEL_TC
+                               ? tc_stages_for(p, (kb + p.split_k - 1) / p.split_k)
+                               : p.stages;
+            if (s2 > 0) p.stages = s2;
             if ((st = fill_derived(m, n, k, &p)) != TINYM_OK) return st;
         }
     }

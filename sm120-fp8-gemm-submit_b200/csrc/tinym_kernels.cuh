@@ -5,9 +5,10 @@
 // The work is cut into 128-row W tiles ("tiles", blockIdx.y) and, when the
 // tiles alone cannot fill the GPU, into split_k contiguous K ranges
 // (blockIdx.x).  The split_k CTAs of one tile form a thread-block cluster and
-// reduce their FP32 partial sums through distributed shared memory into the
-// cluster's rank-0 CTA, which applies alpha and writes BF16 -- a
-// deterministic, single-launch split-K with no global scratch memory.
+// combine their FP32 partial sums through distributed shared memory -- a
+// deterministic, single-launch split-K with no global scratch memory.  The
+// TC kernel reduce-scatters (each CTA sums and stores a block of the tile's
+// rows); the SIMT kernel reduces into the cluster's rank-0 CTA.
 //
 // Two consumers share this skeleton:
 //
@@ -89,8 +90,8 @@ struct SmemLayout {
     uint32_t w_off, x_off, red_off, bar_off, misc_off, bytes;
 };
 
-// red_rank_bytes: split-K partial-sum bytes one non-leader CTA sends to the
-// cluster leader (the leader reserves (split - 1) of them).
+// red_rank_bytes: split-K partial-sum bytes one CTA receives from each other
+// CTA of its cluster (it reserves (split - 1) of them).
 __host__ __device__ inline SmemLayout smem_layout(int stages, int w_stage_bytes, int x_stage_bytes,
                                                   int split, int red_rank_bytes) {
     SmemLayout L;
@@ -111,12 +112,29 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
     return p + (((a + 1023u) & ~1023u) - a);
 }
 
-// Row stride (FP32 elements) of the split-K partial blocks the TC kernel's
-// non-leader CTAs send to their cluster leader: MMA_N values padded by 4 so
-// that the leader's 16-byte shared-memory reads are bank-conflict free.
+// Split-K reduce-scatter of the TC kernel: rank o of a cluster of `split`
+// CTAs owns tile rows [o * rpo, o * rpo + cnt_o), rpo = ceil(tile_m / split)
+// rounded up to 8 rows (whole 16-byte BF16 output vectors), cnt_o = rows
+// left for rank o (0 for trailing ranks when 8-row rounding runs out).
+// Every CTA sends its partial rows to their owners and sums/stores its own.
+__host__ __device__ constexpr int tc_rows_per_owner(int tile_m, int split) {
+    return ((tile_m + split - 1) / split + 7) / 8 * 8;
+}
+__host__ __device__ constexpr int tc_rows_owned(int tile_m, int split, int rank) {
+    return tile_m - rank * tc_rows_per_owner(tile_m, split) <= 0
+               ? 0
+               : (tile_m - rank * tc_rows_per_owner(tile_m, split) <
+                          tc_rows_per_owner(tile_m, split)
+                      ? tile_m - rank * tc_rows_per_owner(tile_m, split)
+                      : tc_rows_per_owner(tile_m, split));
+}
+// Row stride (FP32 elements) of a received partial block: MMA_N values
+// padded by 4 so that 16-byte shared-memory accesses of consecutive rows
+// are bank-conflict free.
 __host__ __device__ constexpr int tc_red_stride(int mma_n) { return mma_n + 4; }
-__host__ __device__ constexpr int tc_red_rank_bytes(int mma_n, int tile_m) {
-    return tile_m * tc_red_stride(mma_n) * 4;
+// Bytes of one received block (one source rank); a CTA holds split - 1.
+__host__ __device__ constexpr int tc_red_rank_bytes(int mma_n, int tile_m, int split) {
+    return tc_rows_per_owner(tile_m, split) * tc_red_stride(mma_n) * 4;
 }
 
 // Named barrier 1 over the 128 epilogue threads (warps 2..5) of the TC kernel.
@@ -153,13 +171,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     constexpr uint32_t kStageTx = kWStage + kXStageBytes;
     constexpr uint32_t kIdesc = idesc_e4m3_f32(TILE_M, MMA_N);
     constexpr int kRedStride = tc_red_stride(MMA_N);
-    constexpr int kRedRankBytes = TILE_M * kRedStride * 4;  // per-rank block in the ring
-    constexpr int kRedSendBytes = TILE_M * MMA_N * 4;       // bytes a rank actually sends
     constexpr int kRowsPerWarp = TILE_M / 4;                // accumulator rows per epilogue warp
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
-    const SmemLayout L = smem_layout(p.stages, kWStage, kXStageBytes, 1, 0);
+    const int red_rank_bytes = tc_red_rank_bytes(MMA_N, TILE_M, p.split);
+    const SmemLayout L = smem_layout(p.stages, kWStage, kXStageBytes, p.split, red_rank_bytes);
     const uint32_t s_base = smem_u32(smem);
     const uint32_t w_ring = s_base + L.w_off;
     const uint32_t x_ring = s_base + L.x_off;
@@ -171,9 +188,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t red_bar = bars + 8u * (2 * stages + 1);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.misc_off);
     volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L.misc_off + 4);
-    // After the mainloop the rings are reused: the leader's W ring receives
-    // the other ranks' partial sums, the X ring stages the BF16 output tile.
-    float* red = reinterpret_cast<float*>(smem + L.w_off);
+    // Partial sums from the other ranks land in their own region; after the
+    // mainloop the X ring stages the BF16 output rows.
+    float* red = reinterpret_cast<float*>(smem + L.red_off);
     __nv_bfloat16* ystage = reinterpret_cast<__nv_bfloat16*>(smem + L.x_off);
 
     const int warp = threadIdx.x >> 5;
@@ -181,7 +198,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int split_idx = blockIdx.x;
     const int tile = blockIdx.y;
     const bool clustered = p.split > 1;
-    const bool leader = split_idx == 0;
+    // Rows of the tile this CTA sums and stores, and the partial-sum columns
+    // that carry data (X rows m < M, in groups of four).
+    const int rpo = tc_rows_per_owner(TILE_M, p.split);
+    const int own_lo = split_idx * rpo;
+    const int own_cnt = tc_rows_owned(TILE_M, p.split, split_idx);
+    const int red_cols = (p.m + 3) & ~3;
     const int kb0 = split_idx * p.kb_per_split;
     const int kb1 = min(kb0 + p.kb_per_split, p.kb_total);
     const int nkb = kb1 - kb0;  // >= 1 by construction of the plan
@@ -237,9 +259,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // as they free up (it still waits for this grid to complete).
         grid_launch_dependents();
         TINYM_TRACE(1);
-        // The cluster leader expects one partial-sum block from each other
-        // CTA of its cluster (st.async, completing bytes on red_bar).
-        if (clustered && leader) mbar_expect_tx(red_bar, (p.split - 1) * kRedSendBytes);
+        // This CTA's rows arrive from every other rank of the cluster
+        // (st.async, completing their bytes on red_bar).
+        if (clustered && own_cnt > 0)
+            mbar_expect_tx(red_bar, static_cast<uint32_t>((p.split - 1) * own_cnt * red_cols * 4));
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(tmem_slot), kTmemCols);
@@ -250,11 +273,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc_fence_after_sync();
     const uint32_t tmem_d = *tmem_slot;
     if (threadIdx.x == 0) TINYM_TRACE(2);
-    // Cluster barrier, one phase: it completes when every non-leader has
-    // started (they arrive now) and the leader's own MMAs have retired (it
-    // arrives after its mainloop), i.e. when the leader's W ring may be
-    // overwritten with partial sums.
-    if (clustered && !leader) cluster_arrive_relaxed();
+    // Cluster barrier, one phase: it completes once every CTA of the cluster
+    // is resident with its barriers initialised (published by
+    // fence.mbarrier_init.release.cluster); waited on only before the first
+    // remote store, long after it has completed.  The arrive is relaxed: a
+    // release arrive here measurably delays the first ring-full's landing.
+    // (red_bar's expect_tx needs no ordering against the remote
+    // complete_tx: the transaction count may go transiently negative.)
+    if (clustered) cluster_arrive_relaxed();
 
     float acc[MMA_N];
     bool have_acc = false;
@@ -320,50 +346,68 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     __syncwarp();
 
-    // ---------------- split-K reduction through distributed shared memory
+    // ---------------- split-K reduce-scatter through distributed shared memory
     // Epilogue thread (warp w, lane t) holds TMEM lane 32*(w%4)+t, which is
     // tile row (w%4)*kRowsPerWarp + t for t < kRowsPerWarp.
     const int row = (warp & 3) * kRowsPerWarp + lane;
     const bool epi = warp >= 2;
     const bool row_ok = epi && lane < kRowsPerWarp;
+    const bool row_mine = row_ok && row >= own_lo && row < own_lo + own_cnt;
     if (clustered) {
-        if (leader) cluster_arrive_release();  // leader's MMAs retired: ring is free
         cluster_wait_acquire();
         if (threadIdx.x == 64) TINYM_TRACE(6);
-        if (row_ok && !leader) {
-            // Push this CTA's partial row block into the leader's ring,
-            // [rank-1][row][kRedStride].  Every epilogue thread always sends
-            // (zeros if it has no accumulator) so the leader's wait ends.
-            const uint32_t dst = dsmem_map(smem_u32(red), 0) +
-                                 static_cast<uint32_t>((split_idx - 1) * kRedRankBytes +
-                                                       row * kRedStride * 4);
-            const uint32_t rbar = dsmem_map(red_bar, 0);
+        if (row_ok && !row_mine) {
+            // Push this row's partial sums to the owner's block for this
+            // rank.  Every such thread always sends (zeros if it has no
+            // accumulator) so the owner's wait ends.
+            const int owner = row / rpo;
+            const int slot = split_idx < owner ? split_idx : split_idx - 1;
+            const uint32_t dst = dsmem_map(smem_u32(red), static_cast<uint32_t>(owner)) +
+                                 static_cast<uint32_t>(slot * red_rank_bytes +
+                                                       (row - owner * rpo) * kRedStride * 4);
+            const uint32_t rbar = dsmem_map(red_bar, static_cast<uint32_t>(owner));
 #pragma unroll
             for (int c = 0; c < MMA_N; c += 4) {
-                float v[4];
+                if (c < red_cols) {
+                    float v[4];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) v[j] = have_acc ? acc[c + j] : 0.f;
-                st_async_v4(dst + 16u * (c / 4), v, rbar);
+                    for (int j = 0; j < 4; ++j) v[j] = have_acc ? acc[c + j] : 0.f;
+                    st_async_v4(dst + 16u * (c / 4), v, rbar);
+                }
             }
-        } else if (row_ok) {
-            // Leader: wait for every other rank's partials (bounded), then
-            // fold them into the accumulator in K order (rank 0 first), so
-            // the result does not depend on arrival order.
+            if (threadIdx.x == 160) TINYM_TRACE(14);
+        } else if (row_mine) {
+            // Owner: wait for the other ranks' partials of this row (bounded),
+            // then add all ranks in K order (rank 0 first), so the result
+            // does not depend on arrival order or on which rank owns the row.
             const bool got = mbar_drain(red_bar, 0, guard, kErrReduceWait);
             if (threadIdx.x == 64) TINYM_TRACE(7);
             if (got && have_acc) {
-                for (int r = 1; r < p.split; ++r) {
-                    const float4* part = reinterpret_cast<const float4*>(
-                        red + (r - 1) * (kRedRankBytes / 4) + row * kRedStride);
+                float sum[MMA_N];
 #pragma unroll
-                    for (int c = 0; c < MMA_N / 4; ++c) {
-                        const float4 q = part[c];
-                        acc[4 * c + 0] += q.x;
-                        acc[4 * c + 1] += q.y;
-                        acc[4 * c + 2] += q.z;
-                        acc[4 * c + 3] += q.w;
+                for (int c = 0; c < MMA_N; ++c) sum[c] = 0.f;
+                for (int r = 0; r < p.split; ++r) {
+                    if (r == split_idx) {
+#pragma unroll
+                        for (int c = 0; c < MMA_N; ++c) sum[c] += acc[c];
+                    } else {
+                        const int slot = r < split_idx ? r : r - 1;
+                        const float4* part = reinterpret_cast<const float4*>(
+                            red + slot * (red_rank_bytes / 4) + (row - own_lo) * kRedStride);
+#pragma unroll
+                        for (int c = 0; c < MMA_N / 4; ++c) {
+                            if (4 * c < red_cols) {
+                                const float4 q = part[c];
+                                sum[4 * c + 0] += q.x;
+                                sum[4 * c + 1] += q.y;
+                                sum[4 * c + 2] += q.z;
+                                sum[4 * c + 3] += q.w;
+                            }
+                        }
                     }
                 }
+#pragma unroll
+                for (int c = 0; c < MMA_N; ++c) acc[c] = sum[c];
             } else {
                 have_acc = false;
             }
@@ -371,21 +415,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
     }
 
-    // ---------------- output: BF16 tile staged in shared memory, then
-    // written row by row with 16-byte stores (8 consecutive N per store).
-    if (epi && (!clustered || leader)) {
-        if (have_acc && row_ok) {
+    // ---------------- output: this CTA's rows, staged in shared memory as
+    // BF16, then written with 16-byte stores (8 consecutive N per store).
+    if (epi) {
+        if (have_acc && row_mine) {
 #pragma unroll
             for (int m = 0; m < MMA_N; ++m)
                 ystage[m * TILE_M + row] = __float2bfloat16_rn(acc[m] * alpha);
         }
+        if (threadIdx.x == 64) TINYM_TRACE(15);
         epilogue_bar_sync();  // the 4 epilogue warps only
+        if (threadIdx.x == 64) TINYM_TRACE(13);
         if (!*abort_flag) {
             const int n0 = tile * TILE_M;
+            const int vecs = own_cnt / 8;  // 16-byte vectors per output row
             const bool vec = ((reinterpret_cast<uintptr_t>(p.y) & 15u) == 0) && (p.ldy % 8 == 0);
-            for (int c = threadIdx.x - 64; c < p.m * (TILE_M / 8); c += 128) {
-                const int m = c / (TILE_M / 8);
-                const int j = (c % (TILE_M / 8)) * 8;
+            for (int c = threadIdx.x - 64; c < p.m * vecs; c += 128) {
+                const int m = c / vecs;
+                const int j = own_lo + (c % vecs) * 8;
                 const __nv_bfloat16* src = ystage + m * TILE_M + j;
                 __nv_bfloat16* dst = p.y + static_cast<size_t>(m) * p.ldy + n0 + j;
                 if (vec && n0 + j + 8 <= p.n) {

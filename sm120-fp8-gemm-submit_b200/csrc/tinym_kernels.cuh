@@ -77,7 +77,21 @@ struct TinymParams {
     int32_t stages;
     uint32_t flags;        // kFlag* bits (0 in normal operation)
     uint64_t timeout_ns;   // limit of every mbarrier wait
+    int32_t w_packed_kc;   // 0: W row-major [N, K]; else W packed, this many K chunks per tile
 };
+
+// Packed weight layout (TC kernel only): W cut into kPackRows-row tiles and
+// 128-byte K chunks; chunk c of tile t is one contiguous [kPackRows][128 B]
+// block at byte offset (t * KC + c) * kPackRows * 128, zero-filled past N
+// and K.  KC = ceil(K / 128) rounded up to a multiple of kPackChunkAlign
+// (the largest stage), so a stage never reaches into the next tile.  A
+// stage of CHUNKS chunks is then a single contiguous HBM range (64 KiB at
+// block_k = 512).
+constexpr int kPackRows = 128;
+constexpr int kPackChunkAlign = 4;
+__host__ __device__ constexpr int64_t packed_chunks(int64_t k) {
+    return ((k + 127) / 128 + kPackChunkAlign - 1) / kPackChunkAlign * kPackChunkAlign;
+}
 
 // TinymParams::flags.  kFlagInjectNoLoads makes the producer issue no TMA
 // copies: nothing ever completes the full barriers, the consumers' bounded
@@ -222,7 +236,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int s = i % stages;
         const int chunk = (kb0 + i) * CHUNKS;  // first 128-byte K chunk of the stage
         mbar_expect_tx(full_bar(s), kStageTx);
-        if constexpr (CHUNKS == 1) {
+        if (p.w_packed_kc) {
+            const int r0 = tile * TILE_M;
+            tma_load_3d(w_ring + s * kWStage, &tm_w, full_bar(s), 0, r0 % kPackRows,
+                        (r0 / kPackRows) * p.w_packed_kc + chunk, pol_w);
+            if constexpr (CHUNKS == 1)
+                tma_load_2d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), chunk * kBlockK, 0, pol_x);
+            else
+                tma_load_3d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), 0, 0, chunk, pol_x);
+        } else if constexpr (CHUNKS == 1) {
             tma_load_2d(w_ring + s * kWStage, &tm_w, full_bar(s), chunk * kBlockK, tile * TILE_M,
                         pol_w);
             tma_load_2d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), chunk * kBlockK, 0, pol_x);
@@ -640,6 +662,27 @@ __global__ void __launch_bounds__(32 * (CWARPS + 1), 1)
         }
     }
     __syncthreads();
+}
+
+// =====================================================================
+// Weight repack into the packed layout (run once, e.g. by prepare_weights)
+// =====================================================================
+// One thread per 16-byte vector of the packed tensor: coalesced stores, and
+// each warp reads two 128-byte row segments of W.
+__global__ void __launch_bounds__(256)
+    tinym_pack_weights_kernel(const uint4* __restrict__ w, uint4* __restrict__ out, int64_t n,
+                              int64_t k, int64_t kc, int64_t total_vecs) {
+    for (int64_t v = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; v < total_vecs;
+         v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t b16 = v & 7;                   // 16-byte column within the chunk
+        const int64_t r = (v >> 3) & (kPackRows - 1);  // row within the tile
+        const int64_t tc = v >> 10;                  // tile * kc + chunk
+        const int64_t row = (tc / kc) * kPackRows + r;
+        const int64_t col = (tc % kc) * 128 + b16 * 16;
+        uint4 val = make_uint4(0u, 0u, 0u, 0u);
+        if (row < n && col < k) val = __ldg(w + (row * k + col) / 16);
+        out[v] = val;
+    }
 }
 
 }  // namespace tinym

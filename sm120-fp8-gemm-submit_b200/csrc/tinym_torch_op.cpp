@@ -5,6 +5,10 @@
 //     sm120_fp8_gemm::run(Tensor a, Tensor b, float alpha) -> Tensor
 // plus a device-alpha form used by candidate_kernel.fp8_gemm:
 //     sm120_fp8_gemm::run_alpha_tensor(Tensor a, Tensor b, Tensor alpha) -> Tensor
+// and the packed-weight pair behind candidate_kernel.prepare_weights'
+// optional repack (tinym_pack_weights / tinym_fp8_gemm_packed):
+//     sm120_fp8_gemm::pack_weights(Tensor b) -> Tensor            (uint8, packed layout)
+//     sm120_fp8_gemm::run_packed(Tensor a, Tensor b_packed, int n, int k, Tensor alpha) -> Tensor
 // Input checks mirror check_inputs (src/torch_candidate_extension.cu:17-31)
 // and raise the same RuntimeError (TORCH_CHECK) messages; shape support is
 // decided by the C ABI (1 <= M <= 16, K % 16 == 0) instead of the six-point
@@ -64,14 +68,61 @@ at::Tensor run_alpha_tensor(const at::Tensor& a, const at::Tensor& b, const at::
     return launch(a, b, alpha.data_ptr<float>(), 0.0f);
 }
 
+at::Tensor pack_weights(const at::Tensor& b) {
+    TORCH_CHECK(b.is_cuda(), "B must be a CUDA tensor");
+    TORCH_CHECK(b.dim() == 2 && b.is_contiguous(), "B must be a contiguous rank-2 tensor");
+    TORCH_CHECK(b.scalar_type() == at::ScalarType::Float8_e4m3fn,
+                "B must have dtype torch.float8_e4m3fn");
+    const int64_t n = b.size(0), k = b.size(1);
+    int64_t bytes = 0;
+    raise_status(tinym_packed_weight_bytes(n, k, &bytes));
+    const c10::cuda::CUDAGuard guard(b.device());
+    at::Tensor out = at::empty({bytes}, b.options().dtype(at::ScalarType::Byte));
+    raise_status(tinym_pack_weights(b.data_ptr(), out.data_ptr(), n, k,
+                                    at::cuda::getCurrentCUDAStream(b.get_device())));
+    return out;
+}
+
+at::Tensor run_packed(const at::Tensor& a, const at::Tensor& bp, int64_t n, int64_t k,
+                      const at::Tensor& alpha) {
+    TORCH_CHECK(a.is_cuda() && bp.is_cuda(), "A and B must be CUDA tensors");
+    TORCH_CHECK(a.get_device() == bp.get_device(), "A and B must be on the same CUDA device");
+    TORCH_CHECK(a.dim() == 2 && a.is_contiguous(), "A must be a contiguous rank-2 tensor");
+    TORCH_CHECK(a.scalar_type() == at::ScalarType::Float8_e4m3fn,
+                "A must have dtype torch.float8_e4m3fn");
+    TORCH_CHECK(a.size(1) == k, "A and B must have the same K dimension");
+    TORCH_CHECK(bp.scalar_type() == at::ScalarType::Byte && bp.dim() == 1 && bp.is_contiguous(),
+                "B_packed must be the uint8 tensor returned by pack_weights");
+    int64_t bytes = 0;
+    raise_status(tinym_packed_weight_bytes(n, k, &bytes));
+    TORCH_CHECK(bp.numel() == bytes, "B_packed has ", bp.numel(), " bytes, packed [", n, ", ",
+                k, "] needs ", bytes);
+    TORCH_CHECK(alpha.is_cuda() && alpha.scalar_type() == at::ScalarType::Float &&
+                    alpha.numel() == 1,
+                "alpha must be a one-element CUDA float32 tensor");
+    TORCH_CHECK(alpha.get_device() == a.get_device(), "alpha must be on A's device");
+    const int64_t m = a.size(0);
+    const c10::cuda::CUDAGuard guard(a.device());
+    at::Tensor y = at::empty({m, n}, a.options().dtype(at::ScalarType::BFloat16));
+    if (m == 0 || n == 0) return y;
+    raise_status(tinym_fp8_gemm_packed(a.data_ptr(), bp.data_ptr(), y.data_ptr(), n, m, n, k,
+                                       alpha.data_ptr<float>(), 0.0f, nullptr,
+                                       at::cuda::getCurrentCUDAStream(a.get_device())));
+    return y;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(sm120_fp8_gemm, module) {
     module.def("run(Tensor a, Tensor b, float alpha) -> Tensor");
     module.def("run_alpha_tensor(Tensor a, Tensor b, Tensor alpha) -> Tensor");
+    module.def("pack_weights(Tensor b) -> Tensor");
+    module.def("run_packed(Tensor a, Tensor b_packed, int n, int k, Tensor alpha) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(sm120_fp8_gemm, CUDA, module) {
     module.impl("run", &run_host_alpha);
     module.impl("run_alpha_tensor", &run_alpha_tensor);
+    module.impl("pack_weights", &pack_weights);
+    module.impl("run_packed", &run_packed);
 }

@@ -51,6 +51,9 @@ EXPORTED = (
     "tinym_device_status",
     "tinym_plan_max_active_clusters",
     "tinym_selftest_wait_timeout",
+    "tinym_packed_weight_bytes",
+    "tinym_pack_weights",
+    "tinym_fp8_gemm_packed",
     "tinym_status_string",
     "tinym_last_error",
     "tinym_abi_version",
@@ -124,6 +127,13 @@ def capi() -> ctypes.CDLL:
             lib.tinym_plan_max_active_clusters.argtypes = [i64, i64, i64, ctypes.POINTER(Plan),
                                                            ctypes.POINTER(ctypes.c_int32)]
             lib.tinym_plan_max_active_clusters.restype = ctypes.c_int
+            lib.tinym_packed_weight_bytes.argtypes = [i64, i64, ctypes.POINTER(i64)]
+            lib.tinym_packed_weight_bytes.restype = ctypes.c_int
+            lib.tinym_pack_weights.argtypes = [vp, vp, i64, i64, vp]
+            lib.tinym_pack_weights.restype = ctypes.c_int
+            lib.tinym_fp8_gemm_packed.argtypes = [vp, vp, vp, i64, i64, i64, i64, vp, f32,
+                                                  ctypes.POINTER(Plan), vp]
+            lib.tinym_fp8_gemm_packed.restype = ctypes.c_int
             lib.tinym_status_string.argtypes = [ctypes.c_int32]
             lib.tinym_status_string.restype = ctypes.c_char_p
             lib.tinym_last_error.argtypes = []
@@ -187,6 +197,27 @@ def gemm_ptr(x_ptr: int, w_ptr: int, y_ptr: int, m: int, n: int, k: int, *,
     st = lib.tinym_fp8_gemm_ex(x_ptr, w_ptr, y_ptr, n if ldy is None else ldy, m, n, k,
                                alpha_ptr, alpha, pl, stream)
     _check(st)
+
+
+def packed_weight_bytes(n: int, k: int) -> int:
+    """Bytes of the packed (tile-contiguous) form of an [N, K] weight."""
+    out = ctypes.c_int64(0)
+    _check(capi().tinym_packed_weight_bytes(n, k, ctypes.byref(out)))
+    return int(out.value)
+
+
+def pack_weights_ptr(w_ptr: int, packed_ptr: int, n: int, k: int, stream: int = 0) -> None:
+    """Repack row-major W [N, K] at w_ptr into the packed layout at packed_ptr."""
+    _check(capi().tinym_pack_weights(w_ptr, packed_ptr, n, k, stream))
+
+
+def gemm_packed_ptr(x_ptr: int, wp_ptr: int, y_ptr: int, m: int, n: int, k: int, *,
+                    ldy: int | None = None, alpha: float = 1.0, alpha_ptr: int | None = None,
+                    plan: Plan | None = None, stream: int = 0) -> None:
+    """Y = alpha * X . W^T with W in the packed layout (tinym_fp8_gemm_packed)."""
+    pl = ctypes.byref(plan) if plan is not None else None
+    _check(capi().tinym_fp8_gemm_packed(x_ptr, wp_ptr, y_ptr, n if ldy is None else ldy, m, n,
+                                        k, alpha_ptr, alpha, pl, stream))
 
 
 def max_active_clusters(m: int, n: int, k: int, plan: Plan) -> int:

@@ -33,7 +33,7 @@ def test_library_exports_every_declared_symbol():
     lib = tinym_b200.capi()
     for name in declared_symbols():
         assert hasattr(lib, name), name
-    assert lib.tinym_abi_version() == 2
+    assert lib.tinym_abi_version() == 3
 
 
 def test_status_strings():
@@ -205,3 +205,17 @@ def test_dispatch_plans_always_validate(m):
             for sms in (148, 132, 40):
                 p = tinym_b200.select_plan(m, n, k, sms)
                 tinym_b200.check_plan(m, n, k, p)
+
+
+def test_packed_weight_bytes():
+    """Packed weights are whole 128-row tiles x a multiple of four 128-byte
+    K chunks."""
+    import tinym_b200 as t
+
+    assert t.packed_weight_bytes(5120, 6144) == 5120 * 6144
+    assert t.packed_weight_bytes(16384, 5120) == 16384 * 5120
+    assert t.packed_weight_bytes(129, 144) == 2 * 4 * 128 * 128
+    assert t.packed_weight_bytes(1, 16) == 4 * 128 * 128
+    assert t.packed_weight_bytes(300, 1152) == 3 * 12 * 128 * 128
+    with pytest.raises(t.TinymError):
+        t.packed_weight_bytes(4, 24)  # K % 16 != 0

@@ -38,7 +38,7 @@ using tinym::TinymParams;
 
 constexpr int kMaxDevices = 64;
 constexpr int kMaxSplit = 8;       // portable cluster size
-constexpr int kMaxStages = 12;
+constexpr int kMaxStages = 32;
 constexpr int kSmemLimit = 232448; // 227 KiB opt-in per CTA on sm_100
 constexpr uint64_t kDefaultTimeoutNs = 1000000000ull;  // 1 s per wait
 
@@ -307,29 +307,40 @@ int max_stages_fitting(const tinym_plan& p, uint32_t limit) {
     return -1;
 }
 
-// Ring depth for a TC plan: as many stages as fit, but no more than the
-// CTA's K blocks (more is useless); -1 if not even two stages fit.
+// W bytes a CTA keeps in flight (ring depth x W stage): 128 KiB measured
+// best on B200 -- deeper rings (192 KiB) lose in the single-launch protocols
+// without gaining back-to-back throughput.
+constexpr int kTargetRingBytes = 128 * 1024;
+
+// Ring depth for a TC plan: kTargetRingBytes of W in flight, at most what
+// fits and at most the CTA's K blocks (more is useless), at least 2; -1 if
+// not even two stages fit.
 int tc_stages_for(const tinym_plan& p, int64_t kb_per_cta) {
     const int max_st = max_stages_fitting(p, static_cast<uint32_t>(kSmemLimit));
     if (max_st < 0) return -1;
-    return static_cast<int>(std::max<int64_t>(2, std::min<int64_t>(kb_per_cta, max_st)));
+    const int64_t want = std::max(2, kTargetRingBytes / w_stage_bytes(p));
+    return static_cast<int>(std::max<int64_t>(2, std::min<int64_t>({kb_per_cta, want, max_st})));
 }
 
 // Heuristic part of the dispatch table, fitted to B200 measurements of the
 // official points (plan sweeps, per-CTA %globaltimer traces):
 //  * one CTA per SM with a deep ring (two CTAs per SM never won);
-//  * block_k = 512 -- one 64 KiB 3-D TMA box of W per stage -- whenever
-//    K % 128 == 0 (a CTA's TMA stream is instruction-bound), else 128;
+//  * block_k = 256 -- one 32 KiB 3-D TMA box of W per stage -- whenever
+//    K % 128 == 0, else 128.  A CTA streams W at ~40 GB/s with 16 KiB
+//    boxes (a per-stage cost that neither ring depth nor a contiguous W
+//    layout removes), while 64 KiB stages make the tensor core's drain of
+//    the last stage (~0.5 us) and the start-up longer; 32 KiB x 4 stages
+//    measured best in the harness protocol at every official point;
 //  * 128-row W tiles (64-row tiles need no K split on N = 5120 / 8192 but
 //    stream only ~37 GB/s per CTA with 32 KiB boxes, which loses);
 //  * the largest K split (cluster size <= 8) that keeps tiles * split CTAs
 //    within one CTA per SM and gives every CTA >= 2 stages;
-//  * as many stages as fit 227 KiB.
+//  * a ring of ~128 KiB of W (tc_stages_for).
 tinym_plan heuristic_plan(int64_t m, int64_t n, int64_t k, int sm_count) {
     tinym_plan p{};
     p.kernel = TINYM_KERNEL_TC;
     p.mma_n = m <= 8 ? 8 : 16;
-    p.block_k = (k % kBlockK == 0) ? 4 * kBlockK : kBlockK;
+    p.block_k = (k % kBlockK == 0) ? 2 * kBlockK : kBlockK;
     p.split_k = 1;
     p.tile_m = kTileRows;
     const int64_t tiles = (n + p.tile_m - 1) / p.tile_m;

@@ -132,15 +132,16 @@ def test_zero_plan_fields_mean_defaults():
 
 
 def test_dispatch_tiles_for_official_points():
-    """The measured winners on B200: 128-row tiles, 64 KiB stages, K split
-    3 / 2 / 1 for N = 5120 / 8192 / 16384."""
+    """The measured winners on B200: 128-row tiles, 32 KiB stages four deep,
+    K split 3 / 2 / 1 for N = 5120 / 8192 / 16384."""
     import tinym_b200 as t
 
     for m in (1, 9, 16):
         for k, n, tile, split in ((6144, 5120, 128, 3), (5120, 8192, 128, 2),
                                   (5120, 16384, 128, 1)):
             p = t.select_plan(m, n, k, 148)
-            assert (p.tile_m, p.split_k, p.block_k) == (tile, split, 512), p.as_dict()
+            assert (p.tile_m, p.split_k, p.block_k, p.stages) == (tile, split, 256, 4), \
+                p.as_dict()
 
 
 def test_block_k_needs_whole_chunks():

@@ -417,7 +417,9 @@ def main():
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_source": f"{peak_note} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
-                         "traffic": committed_traffic(args.workload),
+                         # ncu captures are of the 1-GPU launch; a rank of an
+                         # N-sharded run moves only its slab, so none applies
+                         "traffic": committed_traffic(args.workload) if world == 1 else None,
                          "algorithmic_bytes_per_launch": algo_bytes(m, k, n_local)},
             "gpu_launches": args.steps,
             "clocks": clk.summary(),

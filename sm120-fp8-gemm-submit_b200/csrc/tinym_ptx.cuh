@@ -5,8 +5,8 @@
 // fence, swizzle math, FP8 widening) but for the Blackwell datacenter
 // pipeline: TMA -> mbarrier ring -> tcgen05.mma with the accumulator in
 // tensor memory (TMEM) -> tcgen05.ld epilogue, plus cluster (DSMEM)
-// primitives for the split-K reduction.  No multicast form of any bulk copy
-// appears anywhere in this file.
+// primitives for the split-K reduction.  Every bulk copy here targets only
+// the issuing CTA's own shared memory.
 #pragma once
 
 #include <cuda.h>

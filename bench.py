@@ -296,6 +296,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cublas", action="store_true")
+    ap.add_argument("--no-act", action="store_true", help="skip the fused activation path")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     m, k, n = WORKLOADS[args.workload]
@@ -454,6 +455,59 @@ def main():
                           "(fp8_gemm_task_harness.py:76-96)")
         out["harness_protocol_us"] = hp
         del flush
+
+    # ---- fused activation path (1 GPU): BF16 X quantised per tensor on the
+    # device (quantise prologue + early-W GEMM), same W rotation
+    if rank == 0 and world == 1 and not args.no_act:
+        lib = tinym_b200.capi()
+        xb = [torch.randn(m, k, device=device).to(torch.bfloat16)
+              for _ in range(n_sets)]
+        wsb = [torch.empty(tinym_b200.quant_workspace_bytes(m, k), dtype=torch.uint8,
+                           device=device) for _ in range(n_sets)]
+        act_idx = {id(sset): i for i, sset in enumerate(sets)}
+
+        def act(sset, stream_handle):
+            i = act_idx[id(sset)]
+            x, w, y, sx, sw, alpha = sset
+            st = lib.tinym_fp8_gemm_quant_act(xb[i].data_ptr(), tinym_b200.ACT_BF16,
+                                              w.data_ptr(), sw.data_ptr(), y.data_ptr(), n_local,
+                                              m, n_local, k, wsb[i].data_ptr(), None,
+                                              stream_handle)
+            if st:
+                raise RuntimeError(lib.tinym_last_error().decode())
+
+        for i in range(args.warmup):
+            act(sets[i % n_sets], stream.cuda_stream)
+        per_act = per_launch_latency(act, sets, min(lat_n, 1000))
+        a_steps = min(args.steps, 4000)
+        act_span = graph_throughput(act, sets, a_steps, args.warmup)
+        # the unfused alternative: torch's own per-tensor quantisation
+        # (the harness's quantize_per_tensor ops, fp8_gemm_task_harness.py:41-44)
+        # followed by our GEMM
+        def unfused(sset, stream_handle):
+            i = act_idx[id(sset)]
+            x, w, y, sx, sw, alpha = sset
+            xf = xb[i]
+            scale = (xf.abs().amax().float() / 448.0).clamp(min=1e-12)
+            q = (xf.float() / scale).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+            a2 = (scale * sw).float().reshape(1)
+            tinym_b200.gemm_ptr(q.data_ptr(), w.data_ptr(), y.data_ptr(), m, n_local, k,
+                                alpha_ptr=a2.data_ptr(), stream=stream_handle)
+
+        for i in range(3):
+            unfused(sets[i % n_sets], stream.cuda_stream)
+        per_unf = per_launch_latency(unfused, sets, min(lat_n, 300))
+        out["act_quant_gemm"] = {
+            "input": "bf16 X, per-tensor E4M3 quantisation on the device + GEMM (2 kernels, PDL)",
+            "median_us": round(statistics.median(per_act) * 1e3, 3),
+            "graph_us_per_call": round(act_span / a_steps * 1e3, 3),
+            "plain_gemm_median_us": round(median_us, 3),
+            "plain_gemm_graph_us": round(mean_us, 3),
+            "unfused_torch_quantise_then_gemm_median_us":
+                round(statistics.median(per_unf) * 1e3, 3)}
+        if tinym_b200.device_status():
+            raise SystemExit("device error word set after the fused activation runs")
+        del xb, wsb
 
     # ---- end to end through the public API with host buffers (1 GPU)
     if world == 1 and args.e2e_steps > 0:

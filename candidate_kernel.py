@@ -23,6 +23,10 @@ Differences from the reference adapter:
   the tile-contiguous layout of tinym_pack_weights, which ``fp8_gemm``
   accepts in place of the [N,K] tensor.  The default keeps the reference's
   identity.
+* ``fp8_gemm_act(x, b, w_scale)`` takes the activation before quantisation
+  (BF16 or FP32): the per-tensor E4M3 quantisation of the harness's
+  ``quantize_per_tensor`` (fp8_gemm_task_harness.py:41-44) runs on the device
+  as a prologue overlapped with the GEMM's weight stream.
 
 There is no fallback: if the native library cannot be loaded, ``build()``
 raises.
@@ -50,6 +54,7 @@ _BUILD_LOCK = threading.Lock()
 _run_alpha_tensor = None
 _run_packed = None
 _pack = None
+_run_quant_act = None
 
 
 class PackedWeight:
@@ -72,7 +77,7 @@ class PackedWeight:
 
 def build():
     """Load (building once if needed) the native op; returns True."""
-    global _BUILT, _run_alpha_tensor, _run_packed, _pack
+    global _BUILT, _run_alpha_tensor, _run_packed, _pack, _run_quant_act
     if _BUILT:
         return True
     with _BUILD_LOCK:
@@ -81,6 +86,7 @@ def build():
             _run_alpha_tensor = torch.ops.sm120_fp8_gemm.run_alpha_tensor
             _run_packed = torch.ops.sm120_fp8_gemm.run_packed
             _pack = torch.ops.sm120_fp8_gemm.pack_weights
+            _run_quant_act = torch.ops.sm120_fp8_gemm.run_quant_act
             _BUILT = True
     return True
 
@@ -113,6 +119,15 @@ def fp8_gemm(a: torch.Tensor, b: torch.Tensor, alpha: torch.Tensor) -> torch.Ten
     if isinstance(b, PackedWeight):
         return _run_packed(a, b.data, b.n, b.k, alpha)
     return _run_alpha_tensor(a, b, alpha)
+
+
+def fp8_gemm_act(x: torch.Tensor, b: torch.Tensor, w_scale: torch.Tensor):
+    """Quantise the activation x (BF16/FP32 [M,K]) per tensor on the device and
+    return (bf16(alpha * q(x) @ b.float().T), x_scale) with alpha = x_scale *
+    w_scale.  b is the [N,K] E4M3 weight, w_scale its one-element CUDA scale."""
+    if not _BUILT:
+        build()
+    return _run_quant_act(x, b, w_scale)
 
 
 __all__ = ["build", "prepare_weights", "fp8_gemm"]

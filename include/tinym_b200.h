@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define TINYM_ABI_VERSION 3
+#define TINYM_ABI_VERSION 4
 
 /* Exported-symbol marker (the library is built with hidden visibility). */
 #if defined(__GNUC__)
@@ -167,6 +167,30 @@ TINYM_API int tinym_fp8_gemm_packed(const void* x, const void* w_packed, void* y
                                     int64_t m, int64_t n, int64_t k,
                                     const float* alpha_dev, float alpha,
                                     const tinym_plan* plan, void* stream);
+
+/* Fused activation path (quantise + GEMM).  The caller's step before the
+ * GEMM -- per-tensor E4M3 quantisation of the activation, the harness's
+ * quantize_per_tensor (fp8_gemm_task_harness.py:41-44) -- runs as a
+ * one-cluster prologue kernel that releases the GEMM at once; the GEMM
+ * streams W while X is quantised and waits only before loading X.  The
+ * workspace (tinym_quant_workspace_bytes, 256-byte aligned) receives
+ * x_scale (f32 at byte 0), alpha = x_scale * w_scale (f32 at byte 4) and
+ * the E4M3 codes of X ([M, K] at byte 256).  No reference counterpart: the
+ * reference takes pre-quantised X. */
+#define TINYM_ACT_BF16 1 /* X is [M, K] bfloat16 */
+#define TINYM_ACT_F32 2  /* X is [M, K] float32 */
+
+/* Workspace bytes of tinym_fp8_gemm_quant_act for an [M, K] activation. */
+TINYM_API int tinym_quant_workspace_bytes(int64_t m, int64_t k, int64_t* bytes);
+
+/* Y = bf16(alpha * q(X) . W^T) with q(X), x_scale and alpha computed on the
+ * device from the BF16 / FP32 activation x_act (16-byte aligned) and the
+ * device scalar w_scale_dev.  W is row-major [N, K] E4M3; plan as in
+ * tinym_fp8_gemm_ex (NULL = dispatch table). */
+TINYM_API int tinym_fp8_gemm_quant_act(const void* x_act, int32_t act_dtype, const void* w,
+                                       const float* w_scale_dev, void* y, int64_t ldy,
+                                       int64_t m, int64_t n, int64_t k, void* workspace,
+                                       const tinym_plan* plan, void* stream);
 
 /* Human-readable name of a tinym_status code (static string). */
 TINYM_API const char* tinym_status_string(int32_t status);

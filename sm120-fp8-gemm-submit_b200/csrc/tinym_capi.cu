@@ -28,6 +28,7 @@
 
 #include "../../include/tinym_b200.h"
 #include "tinym_kernels.cuh"
+#include "tinym_quant.cuh"
 
 namespace {
 
@@ -592,6 +593,55 @@ int tinym_fp8_gemm_ex(const void* x, const void* w, void* y, int64_t ldy, int64_
                       void* stream) {
     return gemm_impl(x, w, y, ldy, m, n, k, alpha_dev, alpha, plan, stream, 0u,
                      kDefaultTimeoutNs);
+}
+
+int tinym_quant_workspace_bytes(int64_t m, int64_t k, int64_t* bytes) {
+    t_last_error[0] = '\0';
+    if (!bytes) return fail(TINYM_ERR_INVALID_ARGUMENT, "bytes is NULL");
+    int st = check_shape(m, 1, k);
+    if (st != TINYM_OK) return st;
+    *bytes = tinym::kQuantWsHeader + (m * k + 255) / 256 * 256;
+    return TINYM_OK;
+}
+
+int tinym_fp8_gemm_quant_act(const void* x_act, int32_t act_dtype, const void* w,
+                             const float* w_scale_dev, void* y, int64_t ldy, int64_t m,
+                             int64_t n, int64_t k, void* workspace, const tinym_plan* plan,
+                             void* stream) {
+    t_last_error[0] = '\0';
+    if (!x_act || !w || !w_scale_dev || !y || !workspace)
+        return fail(TINYM_ERR_INVALID_ARGUMENT, "X, W, w_scale, Y and workspace must be non-null");
+    if (act_dtype != TINYM_ACT_BF16 && act_dtype != TINYM_ACT_F32)
+        return fail(TINYM_ERR_INVALID_ARGUMENT, "act_dtype %d is not TINYM_ACT_BF16 / TINYM_ACT_F32",
+                    act_dtype);
+    int st = check_shape(m, n, k);
+    if (st != TINYM_OK) return st;
+    if ((reinterpret_cast<uintptr_t>(x_act) & 15u) || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+        return fail(TINYM_ERR_MISALIGNED, "X must be 16-byte and the workspace 256-byte aligned");
+    if ((reinterpret_cast<uintptr_t>(w_scale_dev) & 3u))
+        return fail(TINYM_ERR_MISALIGNED, "w_scale must be 4-byte aligned");
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    DeviceInfo* di = nullptr;
+    if ((st = device_info(dev, &di)) != TINYM_OK) return st;
+    // Ordinary stream order (no programmatic attribute): everything before
+    // this kernel has completed when it starts, which is what lets the GEMM
+    // read W ahead of its griddepcontrol.wait.
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    auto s = static_cast<cudaStream_t>(stream);
+    if (act_dtype == TINYM_ACT_BF16)
+        tinym::tinym_quant_act_kernel<__nv_bfloat16>
+            <<<tinym::kQuantCtas, tinym::kQuantThreads, 0, s>>>(
+                static_cast<const __nv_bfloat16*>(x_act), m * k, ws, w_scale_dev);
+    else
+        tinym::tinym_quant_act_kernel<float><<<tinym::kQuantCtas, tinym::kQuantThreads, 0, s>>>(
+            static_cast<const float*>(x_act), m * k, ws, w_scale_dev);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "quantise kernel launch");
+    return gemm_impl(ws + tinym::kQuantWsHeader, w, y, ldy, m, n, k,
+                     reinterpret_cast<const float*>(ws) + 1, 0.0f, plan, stream,
+                     tinym::kFlagEarlyW, kDefaultTimeoutNs);
 }
 
 int tinym_packed_weight_bytes(int64_t n, int64_t k, int64_t* bytes) {

@@ -98,6 +98,13 @@ __host__ __device__ constexpr int64_t packed_chunks(int64_t k) {
 // waits run out, and the kernel reports through g_err_word and exits
 // cleanly.  Used only by the failure-detection self-test.
 constexpr uint32_t kFlagInjectNoLoads = 1u;
+// kFlagEarlyW: the previous kernel in the stream (launched without the
+// programmatic-serialisation attribute, so everything before it has
+// completed) writes only X and alpha -- the fused activation-quantise
+// prologue.  The producer then puts the first ring-full of W loads in
+// flight before griddepcontrol.wait and only the X loads after it, so W
+// streams while X is being quantised.
+constexpr uint32_t kFlagEarlyW = 2u;
 
 // Shared-memory carve-up, identical on host (size) and device (offsets).
 struct SmemLayout {
@@ -232,7 +239,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // bytes overlaps the TMEM allocation and the CTA-wide sync below.
     int issued = 0;
     uint64_t pol_w = 0, pol_x = 0;
-    auto issue = [&](int i) {
+    // One stage = expect_tx(W + X bytes), then the W box and the X box on the
+    // stage's full barrier (issue_w posts the expect_tx).
+    auto issue_w = [&](int i) {
         const int s = i % stages;
         const int chunk = (kb0 + i) * CHUNKS;  // first 128-byte K chunk of the stage
         mbar_expect_tx(full_bar(s), kStageTx);
@@ -240,18 +249,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int r0 = tile * TILE_M;
             tma_load_3d(w_ring + s * kWStage, &tm_w, full_bar(s), 0, r0 % kPackRows,
                         (r0 / kPackRows) * p.w_packed_kc + chunk, pol_w);
-            if constexpr (CHUNKS == 1)
-                tma_load_2d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), chunk * kBlockK, 0, pol_x);
-            else
-                tma_load_3d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), 0, 0, chunk, pol_x);
         } else if constexpr (CHUNKS == 1) {
             tma_load_2d(w_ring + s * kWStage, &tm_w, full_bar(s), chunk * kBlockK, tile * TILE_M,
                         pol_w);
-            tma_load_2d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), chunk * kBlockK, 0, pol_x);
         } else {
             tma_load_3d(w_ring + s * kWStage, &tm_w, full_bar(s), 0, tile * TILE_M, chunk, pol_w);
-            tma_load_3d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), 0, 0, chunk, pol_x);
         }
+    };
+    auto issue_x = [&](int i) {
+        const int s = i % stages;
+        const int chunk = (kb0 + i) * CHUNKS;
+        if constexpr (CHUNKS == 1)
+            tma_load_2d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), chunk * kBlockK, 0, pol_x);
+        else
+            tma_load_3d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), 0, 0, chunk, pol_x);
+    };
+    auto issue = [&](int i) {
+        issue_w(i);
+        issue_x(i);
     };
     if (threadIdx.x == 0) {
         TINYM_TRACE(0);
@@ -271,11 +286,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         pol_x = l2_policy_evict_last();
         // Programmatic dependent launch: everything above overlaps the
         // previous kernel's tail; no global memory is read before it has
-        // completed and its writes are visible.
-        grid_dependency_wait();
-        for (; issued < min(stages, n_issue); ++issued) {
-            issue(issued);
-            if (issued == 0) TINYM_TRACE(11);
+        // completed and its writes are visible -- except W under
+        // kFlagEarlyW, which that kernel does not write.
+        const int first = min(stages, n_issue);
+        if (p.flags & kFlagEarlyW) {
+            for (int i = 0; i < first; ++i) issue_w(i);
+            grid_dependency_wait();
+            for (; issued < first; ++issued) issue_x(issued);
+        } else {
+            grid_dependency_wait();
+            for (; issued < first; ++issued) {
+                issue(issued);
+                if (issued == 0) TINYM_TRACE(11);
+            }
         }
         // Let the next kernel in the stream start its own prologue on SMs
         // as they free up (it still waits for this grid to complete).

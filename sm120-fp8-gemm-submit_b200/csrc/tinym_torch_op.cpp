@@ -9,6 +9,9 @@
 // optional repack (tinym_pack_weights / tinym_fp8_gemm_packed):
 //     sm120_fp8_gemm::pack_weights(Tensor b) -> Tensor            (uint8, packed layout)
 //     sm120_fp8_gemm::run_packed(Tensor a, Tensor b_packed, int n, int k, Tensor alpha) -> Tensor
+// and the fused activation path (tinym_fp8_gemm_quant_act): a BF16 / FP32
+// activation quantised per tensor on the device, then the GEMM:
+//     sm120_fp8_gemm::run_quant_act(Tensor x, Tensor b, Tensor w_scale) -> (Tensor y, Tensor x_scale)
 // Input checks mirror check_inputs (src/torch_candidate_extension.cu:17-31)
 // and raise the same RuntimeError (TORCH_CHECK) messages; shape support is
 // decided by the C ABI (1 <= M <= 16, K % 16 == 0) instead of the six-point
@@ -111,6 +114,33 @@ at::Tensor run_packed(const at::Tensor& a, const at::Tensor& bp, int64_t n, int6
     return y;
 }
 
+std::tuple<at::Tensor, at::Tensor> run_quant_act(const at::Tensor& x, const at::Tensor& b,
+                                                 const at::Tensor& w_scale) {
+    TORCH_CHECK(x.is_cuda() && b.is_cuda() && w_scale.is_cuda(), "X, B and w_scale must be CUDA tensors");
+    TORCH_CHECK(x.get_device() == b.get_device() && w_scale.get_device() == b.get_device(),
+                "X, B and w_scale must be on the same CUDA device");
+    TORCH_CHECK(x.dim() == 2 && b.dim() == 2, "X and B must both be rank-2 tensors");
+    TORCH_CHECK(x.is_contiguous() && b.is_contiguous(), "X and B must be contiguous row-major tensors");
+    TORCH_CHECK(x.scalar_type() == at::ScalarType::BFloat16 || x.scalar_type() == at::ScalarType::Float,
+                "X must have dtype torch.bfloat16 or torch.float32");
+    TORCH_CHECK(b.scalar_type() == at::ScalarType::Float8_e4m3fn, "B must have dtype torch.float8_e4m3fn");
+    TORCH_CHECK(x.size(1) == b.size(1), "X and B must have the same K dimension");
+    TORCH_CHECK(w_scale.scalar_type() == at::ScalarType::Float && w_scale.numel() == 1,
+                "w_scale must be a one-element float32 tensor");
+    const int64_t m = x.size(0), k = x.size(1), n = b.size(0);
+    const c10::cuda::CUDAGuard guard(x.device());
+    at::Tensor y = at::empty({m, n}, b.options().dtype(at::ScalarType::BFloat16));
+    int64_t ws_bytes = 0;
+    raise_status(tinym_quant_workspace_bytes(m, k, &ws_bytes));
+    at::Tensor ws = at::empty({ws_bytes}, b.options().dtype(at::ScalarType::Byte));
+    const int dt = x.scalar_type() == at::ScalarType::BFloat16 ? TINYM_ACT_BF16 : TINYM_ACT_F32;
+    raise_status(tinym_fp8_gemm_quant_act(x.data_ptr(), dt, b.data_ptr(), w_scale.data_ptr<float>(),
+                                          y.data_ptr(), n, m, n, k, ws.data_ptr(), nullptr,
+                                          at::cuda::getCurrentCUDAStream(x.get_device())));
+    // x_scale is the workspace's first float (a view keeps the workspace alive).
+    return {y, ws.narrow(0, 0, 4).view(at::ScalarType::Float)};
+}
+
 }  // namespace
 
 TORCH_LIBRARY(sm120_fp8_gemm, module) {
@@ -118,6 +148,7 @@ TORCH_LIBRARY(sm120_fp8_gemm, module) {
     module.def("run_alpha_tensor(Tensor a, Tensor b, Tensor alpha) -> Tensor");
     module.def("pack_weights(Tensor b) -> Tensor");
     module.def("run_packed(Tensor a, Tensor b_packed, int n, int k, Tensor alpha) -> Tensor");
+    module.def("run_quant_act(Tensor x, Tensor b, Tensor w_scale) -> (Tensor, Tensor)");
 }
 
 TORCH_LIBRARY_IMPL(sm120_fp8_gemm, CUDA, module) {
@@ -125,4 +156,5 @@ TORCH_LIBRARY_IMPL(sm120_fp8_gemm, CUDA, module) {
     module.impl("run_alpha_tensor", &run_alpha_tensor);
     module.impl("pack_weights", &pack_weights);
     module.impl("run_packed", &run_packed);
+    module.impl("run_quant_act", &run_quant_act);
 }

@@ -54,6 +54,8 @@ EXPORTED = (
     "tinym_packed_weight_bytes",
     "tinym_pack_weights",
     "tinym_fp8_gemm_packed",
+    "tinym_quant_workspace_bytes",
+    "tinym_fp8_gemm_quant_act",
     "tinym_status_string",
     "tinym_last_error",
     "tinym_abi_version",
@@ -134,6 +136,11 @@ def capi() -> ctypes.CDLL:
             lib.tinym_fp8_gemm_packed.argtypes = [vp, vp, vp, i64, i64, i64, i64, vp, f32,
                                                   ctypes.POINTER(Plan), vp]
             lib.tinym_fp8_gemm_packed.restype = ctypes.c_int
+            lib.tinym_quant_workspace_bytes.argtypes = [i64, i64, ctypes.POINTER(i64)]
+            lib.tinym_quant_workspace_bytes.restype = ctypes.c_int
+            lib.tinym_fp8_gemm_quant_act.argtypes = [vp, ctypes.c_int32, vp, vp, vp, i64, i64, i64,
+                                                     i64, vp, ctypes.POINTER(Plan), vp]
+            lib.tinym_fp8_gemm_quant_act.restype = ctypes.c_int
             lib.tinym_status_string.argtypes = [ctypes.c_int32]
             lib.tinym_status_string.restype = ctypes.c_char_p
             lib.tinym_last_error.argtypes = []
@@ -220,6 +227,43 @@ def gemm_packed_ptr(x_ptr: int, wp_ptr: int, y_ptr: int, m: int, n: int, k: int,
                                         k, alpha_ptr, alpha, pl, stream))
 
 
+ACT_BF16 = 1
+ACT_F32 = 2
+
+
+def quant_workspace_bytes(m: int, k: int) -> int:
+    """Workspace bytes of the fused activation path for an [M, K] activation."""
+    out = ctypes.c_int64(0)
+    _check(capi().tinym_quant_workspace_bytes(m, k, ctypes.byref(out)))
+    return int(out.value)
+
+
+def gemm_quant_act(x, w, w_scale, *, out=None, workspace=None, plan: Plan | None = None):
+    """Fused activation path: quantise BF16 / FP32 x per tensor on the device,
+    then Y = alpha * q(x) . W^T.  Returns (Y, workspace); the workspace holds
+    x_scale, alpha and the E4M3 codes (see include/tinym_b200.h)."""
+    import torch
+
+    if x.dtype == torch.bfloat16:
+        dt = ACT_BF16
+    elif x.dtype == torch.float32:
+        dt = ACT_F32
+    else:
+        raise ValueError("x must be bfloat16 or float32")
+    m, k = x.shape
+    n = w.shape[0]
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    if workspace is None:
+        workspace = torch.empty(quant_workspace_bytes(m, k), dtype=torch.uint8, device=x.device)
+    stream = torch.cuda.current_stream(x.device).cuda_stream
+    pl = ctypes.byref(plan) if plan is not None else None
+    _check(capi().tinym_fp8_gemm_quant_act(x.data_ptr(), dt, w.data_ptr(), w_scale.data_ptr(),
+                                           out.data_ptr(), out.stride(0), m, n, k,
+                                           workspace.data_ptr(), pl, stream))
+    return out, workspace
+
+
 def max_active_clusters(m: int, n: int, k: int, plan: Plan) -> int:
     """Clusters of `plan` the current GPU can hold resident at once."""
     out = ctypes.c_int32(0)
@@ -259,4 +303,6 @@ def gemm(x, w, alpha, *, out=None, plan: Plan | None = None):
 __all__ = [
     "capi", "load_torch_op", "select_plan", "check_plan", "make_plan", "gemm_ptr", "gemm",
     "device_status", "Plan", "TinymError", "EXPORTED", "KERNEL_TC", "KERNEL_SIMT_M1",
+    "packed_weight_bytes", "pack_weights_ptr", "gemm_packed_ptr", "quant_workspace_bytes",
+    "gemm_quant_act", "ACT_BF16", "ACT_F32",
 ]

@@ -32,6 +32,7 @@ TORCH_SO = LIBDIR / "tinym_torch_op.so"
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CORE_SOURCES = [CSRC / "tinym_capi.cu"]
 CORE_DEPS = CORE_SOURCES + [CSRC / "tinym_kernels.cuh", CSRC / "tinym_ptx.cuh",
+                            CSRC / "tinym_quant.cuh",
                             INCLUDE / "tinym_b200.h"]
 TORCH_SOURCES = [CSRC / "tinym_torch_op.cpp"]
 

@@ -192,6 +192,18 @@ TINYM_API int tinym_fp8_gemm_quant_act(const void* x_act, int32_t act_dtype, con
                                        int64_t m, int64_t n, int64_t k, void* workspace,
                                        const tinym_plan* plan, void* stream);
 
+/* tinym_fp8_gemm_quant_act without a caller-provided workspace: the
+ * workspace is a static device array inside the library (its address found
+ * per device with cudaGetSymbolAddress), so the call allocates nothing and
+ * needs no workspace argument.  M * K must be at most 524288 (else
+ * TINYM_ERR_UNSUPPORTED_SHAPE).  The array is shared by every call on a
+ * device: calls must be ordered on one stream (or otherwise serialised);
+ * x_scale and alpha can be read back only until the next such call. */
+TINYM_API int tinym_fp8_gemm_quant_act_noalloc(const void* x_act, int32_t act_dtype,
+                                               const void* w, const float* w_scale_dev,
+                                               void* y, int64_t ldy, int64_t m, int64_t n,
+                                               int64_t k, const tinym_plan* plan, void* stream);
+
 /* Human-readable name of a tinym_status code (static string). */
 TINYM_API const char* tinym_status_string(int32_t status);
 

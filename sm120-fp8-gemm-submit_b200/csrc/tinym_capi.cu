@@ -464,6 +464,25 @@ int max_active_clusters(const tinym_plan& p, int dev, DeviceInfo* di, int* out) 
     return TINYM_OK;
 }
 
+// Workspace of the no-allocation form of the fused activation path: a
+// file-scope device array (one per device context), sized for M * K up to
+// kNoAllocMaxElems.  Its address is taken once per device with
+// cudaGetSymbolAddress.
+constexpr int64_t kNoAllocMaxElems = int64_t(16) * 32768;
+static __device__ __align__(256) uint8_t g_quant_scratch[tinym::kQuantWsHeader + kNoAllocMaxElems];
+std::atomic<void*> g_scratch_addr[kMaxDevices];
+
+int scratch_address(int dev, void** out) {
+    void* p = g_scratch_addr[dev].load(std::memory_order_acquire);
+    if (!p) {
+        cudaError_t e = cudaGetSymbolAddress(&p, g_quant_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(scratch)");
+        g_scratch_addr[dev].store(p, std::memory_order_release);
+    }
+    *out = p;
+    return TINYM_OK;
+}
+
 }  // namespace
 
 // =====================================================================
@@ -642,6 +661,26 @@ int tinym_fp8_gemm_quant_act(const void* x_act, int32_t act_dtype, const void* w
     return gemm_impl(ws + tinym::kQuantWsHeader, w, y, ldy, m, n, k,
                      reinterpret_cast<const float*>(ws) + 1, 0.0f, plan, stream,
                      tinym::kFlagEarlyW, kDefaultTimeoutNs);
+}
+
+int tinym_fp8_gemm_quant_act_noalloc(const void* x_act, int32_t act_dtype, const void* w,
+                                     const float* w_scale_dev, void* y, int64_t ldy, int64_t m,
+                                     int64_t n, int64_t k, const tinym_plan* plan, void* stream) {
+    t_last_error[0] = '\0';
+    int st = check_shape(m, n, k);
+    if (st != TINYM_OK) return st;
+    if (m * k > kNoAllocMaxElems)
+        return fail(TINYM_ERR_UNSUPPORTED_SHAPE,
+                    "M*K = %lld exceeds the static workspace (%lld elements)",
+                    static_cast<long long>(m * k), static_cast<long long>(kNoAllocMaxElems));
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= kMaxDevices) return fail(TINYM_ERR_CUDA, "device ordinal %d out of range", dev);
+    void* ws = nullptr;
+    if ((st = scratch_address(dev, &ws)) != TINYM_OK) return st;
+    return tinym_fp8_gemm_quant_act(x_act, act_dtype, w, w_scale_dev, y, ldy, m, n, k, ws, plan,
+                                    stream);
 }
 
 int tinym_packed_weight_bytes(int64_t n, int64_t k, int64_t* bytes) {

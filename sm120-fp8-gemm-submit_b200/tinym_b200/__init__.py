@@ -56,6 +56,7 @@ EXPORTED = (
     "tinym_fp8_gemm_packed",
     "tinym_quant_workspace_bytes",
     "tinym_fp8_gemm_quant_act",
+    "tinym_fp8_gemm_quant_act_noalloc",
     "tinym_status_string",
     "tinym_last_error",
     "tinym_abi_version",
@@ -141,6 +142,10 @@ def capi() -> ctypes.CDLL:
             lib.tinym_fp8_gemm_quant_act.argtypes = [vp, ctypes.c_int32, vp, vp, vp, i64, i64, i64,
                                                      i64, vp, ctypes.POINTER(Plan), vp]
             lib.tinym_fp8_gemm_quant_act.restype = ctypes.c_int
+            lib.tinym_fp8_gemm_quant_act_noalloc.argtypes = [vp, ctypes.c_int32, vp, vp, vp, i64,
+                                                             i64, i64, i64,
+                                                             ctypes.POINTER(Plan), vp]
+            lib.tinym_fp8_gemm_quant_act_noalloc.restype = ctypes.c_int
             lib.tinym_status_string.argtypes = [ctypes.c_int32]
             lib.tinym_status_string.restype = ctypes.c_char_p
             lib.tinym_last_error.argtypes = []

@@ -297,6 +297,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cublas", action="store_true")
     ap.add_argument("--no-act", action="store_true", help="skip the fused activation path")
+    ap.add_argument("--no-fused-gather", action="store_true",
+                    help="N > 1: skip the fused all-gather comparison")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     m, k, n = WORKLOADS[args.workload]
@@ -318,6 +320,9 @@ def main():
 
         import torch.distributed as dist
 
+        # NCCL's log (its version banner included) goes to stderr, so stdout
+        # carries only the bench line.
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=device)
 
@@ -389,6 +394,58 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         allgather_us = float(t.item())
 
+    # GEMM + gather of Y on every rank, two ways, per call on the device
+    # (a spacer covers the host's enqueueing; max over ranks): NCCL
+    # all-gather after the GEMM, and the gather fused into the GEMM's
+    # epilogue (peer stores + arrival counters, tinym_fp8_gemm_allgather).
+    gather_cmp = None
+    if dist is not None and not args.no_fused_gather:
+        from tinym_b200.sharded import ShardedFp8Gemm
+
+        iters = 50
+
+        def device_time(step):
+            for i in range(5):
+                step(i)
+            torch.cuda.synchronize()
+            dist.barrier()
+            torch.cuda._sleep(SPACER_CYCLES * iters)  # ~0.05 ms of spin per call
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(iters):
+                step(i)
+            e1.record()
+            torch.cuda.synchronize()
+            tt = torch.tensor([e0.elapsed_time(e1) / iters * 1e3], device=device,
+                              dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            return float(tt.item())
+
+        gather_cmp = {"protocol": f"{iters} back-to-back calls after a spacer, cold W "
+                                  "(rotating slabs), device time, max over ranks"}
+        y_full = torch.empty(world * m * n_local, device=device, dtype=torch.bfloat16)
+
+        def nccl_step(i):
+            ours(sets[i % n_sets], stream.cuda_stream)
+            dist.all_gather_into_tensor(y_full, sets[i % n_sets][2].reshape(-1))
+
+        gather_cmp["gemm_plus_nccl_allgather_us"] = round(device_time(nccl_step), 3)
+        try:
+            g = ShardedFp8Gemm(sets[0][1], n, rank * n_local, (rank + 1) * n_local)
+            g.enable_fused_gather(m_max=m, device=device)
+
+            def fused_step(i):
+                g.w_local = sets[i % n_sets][1]
+                g.fused(sets[i % n_sets][0], sets[i % n_sets][5])
+
+            gather_cmp["gemm_fused_allgather_us"] = round(device_time(fused_step), 3)
+            err_word = tinym_b200.device_status()
+            g.close_fused_gather()
+            if err_word:
+                gather_cmp["error"] = f"device error word 0x{err_word:x}"
+        except Exception as e:  # reported, not fatal to the main measurement
+            gather_cmp["error"] = f"{type(e).__name__}: {e}"
+
     out = None
     if rank == 0:
         peaks = measured_peaks()
@@ -427,6 +484,8 @@ def main():
         }
         if allgather_us is not None:
             out["allgather_us"] = round(allgather_us, 2)
+        if gather_cmp is not None:
+            out["gather_of_y"] = gather_cmp
 
     # ---- cuBLASLt competitor (1 GPU only, same buffers / protocol)
     if rank == 0 and world == 1 and not args.no_cublas:

@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define TINYM_ABI_VERSION 4
+#define TINYM_ABI_VERSION 5
 
 /* Exported-symbol marker (the library is built with hidden visibility). */
 #if defined(__GNUC__)
@@ -203,6 +203,46 @@ TINYM_API int tinym_fp8_gemm_quant_act_noalloc(const void* x_act, int32_t act_dt
                                                const void* w, const float* w_scale_dev,
                                                void* y, int64_t ldy, int64_t m, int64_t n,
                                                int64_t k, const tinym_plan* plan, void* stream);
+
+/* Fused all-gather of the N-sharded (column-parallel) wrapper.  Rank r owns
+ * W rows [col0, col0 + n_local) and, instead of writing a local slab that a
+ * collective then gathers, its GEMM epilogue stores the BF16 rows straight
+ * into every rank's full Y [M, n_full] (plain stores through CUDA IPC
+ * mappings over NVLink) and then adds the number of elements it stored to
+ * every rank's 64-bit arrival counter (release, system scope).  One CTA of
+ * the GEMM waits (acquire, bounded: 1 s, then bit 0x40 of the device error
+ * word) until this rank's counter reaches `target`, so the GEMM completes
+ * only when this rank's full Y is present; the grid must fit the GPU in one
+ * wave (else TINYM_ERR_BAD_PLAN).
+ * Counters only grow: every call adds M * n_full to every rank's counter,
+ * so target = the sum of M * n_full over this and all earlier calls (the
+ * same on every rank, which make the same calls in the same order).  Two Y
+ * buffers used alternately (by e's parity) keep a fast rank's next call
+ * from overwriting a result another rank is still reading, provided each
+ * rank's readers of Y are stream-ordered before its next call.  No
+ * reference counterpart: the reference is single-GPU. */
+typedef struct tinym_gather_desc {
+    int32_t world;      /* ranks, 1..8 */
+    int32_t rank;       /* this rank */
+    int64_t n_full;     /* columns (and row stride) of the full Y */
+    int64_t col0;       /* first column of this rank's slab */
+    void* y_full[8];    /* every rank's full Y for this call, mapped into this process */
+    void* flag[8];      /* every rank's 8-byte arrival counter, mapped into this process */
+    uint64_t target;    /* this rank's counter once the gather of this call is complete */
+} tinym_gather_desc;
+
+/* Y_full (on every rank) = alpha * X . W^T, W N-sharded across the ranks. */
+TINYM_API int tinym_fp8_gemm_allgather(const void* x, const void* w_local, int64_t m,
+                                       int64_t n_local, int64_t k, const float* alpha_dev,
+                                       float alpha, const tinym_gather_desc* gd,
+                                       const tinym_plan* plan, void* stream);
+
+/* CUDA IPC helpers for the descriptor: the handle (64 bytes) of the
+ * allocation that holds ptr and ptr's offset in it; open / close a peer's
+ * handle in this process. */
+TINYM_API int tinym_ipc_export(const void* ptr, void* handle, int64_t* offset);
+TINYM_API int tinym_ipc_open(const void* handle, void** base);
+TINYM_API int tinym_ipc_close(void* base);
 
 /* Human-readable name of a tinym_status code (static string). */
 TINYM_API const char* tinym_status_string(int32_t status);

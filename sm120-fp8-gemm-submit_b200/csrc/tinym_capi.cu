@@ -74,6 +74,23 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
 cudaError_t g_encode_err = cudaSuccess;
 
+// cuMemGetAddressRange (driver API, fetched like the encoder): the base of
+// the allocation that holds a pointer, for CUDA IPC export.
+using AddrRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+AddrRangeFn get_addr_range() {
+    static std::once_flag once;
+    static AddrRangeFn fn_ptr = nullptr;
+    std::call_once(once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn_ptr = reinterpret_cast<AddrRangeFn>(fn);
+    });
+    return fn_ptr;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
     std::call_once(g_encode_once, [] {
         void* fn = nullptr;
@@ -528,7 +545,8 @@ int tinym_select_plan(int64_t m, int64_t n, int64_t k, int32_t sm_count, tinym_p
 
 static int gemm_impl(const void* x, const void* w, void* y, int64_t ldy, int64_t m, int64_t n,
                      int64_t k, const float* alpha_dev, float alpha, const tinym_plan* plan,
-                     void* stream, uint32_t flags, uint64_t timeout_ns, bool w_packed = false) {
+                     void* stream, uint32_t flags, uint64_t timeout_ns, bool w_packed = false,
+                     const tinym_gather_desc* gd = nullptr) {
     t_last_error[0] = '\0';
     if (!x || !w || !y) return fail(TINYM_ERR_INVALID_ARGUMENT, "X, W and Y must be non-null");
     int st = check_shape(m, n, k);
@@ -570,6 +588,8 @@ static int gemm_impl(const void* x, const void* w, void* y, int64_t ldy, int64_t
 
     if (w_packed && p.kernel != TINYM_KERNEL_TC)
         return fail(TINYM_ERR_BAD_PLAN, "packed weights need the TC kernel");
+    if (gd && p.kernel != TINYM_KERNEL_TC)
+        return fail(TINYM_ERR_BAD_PLAN, "the fused all-gather needs the TC kernel");
     CUtensorMap tm_w, tm_x;
     const int chunks = plan_chunks(p);
     if ((st = get_map(w, n, k, p.tile_m, 1, chunks, dev, &tm_w, w_packed ? 1 : 0)) != TINYM_OK)
@@ -595,6 +615,23 @@ static int gemm_impl(const void* x, const void* w, void* y, int64_t ldy, int64_t
     prm.flags = flags;
     prm.timeout_ns = timeout_ns;
     prm.w_packed_kc = w_packed ? static_cast<int32_t>(tinym::packed_chunks(k)) : 0;
+    if (gd) {
+        // CTA (0,0) waits for the other ranks: the whole grid must be resident
+        // at once, or a waiting CTA could hold an SM another CTA needs.
+        int resident = 0;
+        if ((st = max_active_clusters(p, dev, di, &resident)) != TINYM_OK) return st;
+        if (resident < p.tiles_n)
+            return fail(TINYM_ERR_BAD_PLAN,
+                        "the fused all-gather needs the whole grid resident (%d of %d %s)",
+                        resident, p.tiles_n, p.split_k > 1 ? "clusters" : "CTAs");
+        prm.n_peers = gd->world;
+        prm.rank = gd->rank;
+        prm.gather_target = gd->target;
+        for (int r = 0; r < gd->world; ++r) {
+            prm.peer_y[r] = static_cast<__nv_bfloat16*>(gd->y_full[r]) + gd->col0;
+            prm.peer_flag[r] = static_cast<unsigned long long*>(gd->flag[r]);
+        }
+    }
 
     const void* fn = nullptr;
     if ((st = kernel_for(p, di, &fn)) != TINYM_OK) return st;
@@ -681,6 +718,59 @@ int tinym_fp8_gemm_quant_act_noalloc(const void* x_act, int32_t act_dtype, const
     if ((st = scratch_address(dev, &ws)) != TINYM_OK) return st;
     return tinym_fp8_gemm_quant_act(x_act, act_dtype, w, w_scale_dev, y, ldy, m, n, k, ws, plan,
                                     stream);
+}
+
+int tinym_ipc_export(const void* ptr, void* handle, int64_t* offset) {
+    t_last_error[0] = '\0';
+    if (!ptr || !handle || !offset) return fail(TINYM_ERR_INVALID_ARGUMENT, "null argument");
+    AddrRangeFn range = get_addr_range();
+    if (!range) return fail(TINYM_ERR_CUDA, "cuMemGetAddressRange unavailable");
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+        return fail(TINYM_ERR_CUDA, "cuMemGetAddressRange failed for %p", ptr);
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+    std::memcpy(handle, &h, sizeof(h));
+    *offset = static_cast<int64_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+    return TINYM_OK;
+}
+
+int tinym_ipc_open(const void* handle, void** base) {
+    t_last_error[0] = '\0';
+    if (!handle || !base) return fail(TINYM_ERR_INVALID_ARGUMENT, "null argument");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    cudaError_t e = cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+    return TINYM_OK;
+}
+
+int tinym_ipc_close(void* base) {
+    t_last_error[0] = '\0';
+    cudaError_t e = cudaIpcCloseMemHandle(base);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
+    return TINYM_OK;
+}
+
+int tinym_fp8_gemm_allgather(const void* x, const void* w_local, int64_t m, int64_t n_local,
+                             int64_t k, const float* alpha_dev, float alpha,
+                             const tinym_gather_desc* gd, const tinym_plan* plan, void* stream) {
+    t_last_error[0] = '\0';
+    if (!gd) return fail(TINYM_ERR_INVALID_ARGUMENT, "gather descriptor is NULL");
+    if (gd->world < 1 || gd->world > tinym::kMaxPeers || gd->rank < 0 || gd->rank >= gd->world)
+        return fail(TINYM_ERR_INVALID_ARGUMENT, "world %d / rank %d out of range (1..%d ranks)",
+                    gd->world, gd->rank, tinym::kMaxPeers);
+    if (gd->col0 < 0 || gd->col0 + n_local > gd->n_full)
+        return fail(TINYM_ERR_INVALID_ARGUMENT, "columns [%lld, %lld) exceed N_full %lld",
+                    (long long)gd->col0, (long long)(gd->col0 + n_local), (long long)gd->n_full);
+    for (int r = 0; r < gd->world; ++r)
+        if (!gd->y_full[r] || !gd->flag[r] || (reinterpret_cast<uintptr_t>(gd->flag[r]) & 7u))
+            return fail(TINYM_ERR_INVALID_ARGUMENT, "rank %d: null Y or unaligned counter", r);
+    return gemm_impl(x, w_local, static_cast<__nv_bfloat16*>(gd->y_full[gd->rank]) + gd->col0,
+                     gd->n_full, m, n_local, k, alpha_dev, alpha, plan, stream, 0u,
+                     kDefaultTimeoutNs, false, gd);
 }
 
 int tinym_packed_weight_bytes(int64_t n, int64_t k, int64_t* bytes) {

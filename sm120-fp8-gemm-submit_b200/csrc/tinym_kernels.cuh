@@ -58,6 +58,7 @@ enum : uint32_t {
     kErrDrain = 1u << 3,
     kErrConsumerWait = 1u << 4,
     kErrReduceWait = 1u << 5,
+    kErrPeerWait = 1u << 6,
 };
 
 constexpr int kTileRows = 128;   // W rows per tile of the SIMT kernel (and the TC default)
@@ -78,7 +79,19 @@ struct TinymParams {
     uint32_t flags;        // kFlag* bits (0 in normal operation)
     uint64_t timeout_ns;   // limit of every mbarrier wait
     int32_t w_packed_kc;   // 0: W row-major [N, K]; else W packed, this many K chunks per tile
+    // Fused all-gather of the N-sharded wrapper (n_peers > 0): the BF16 rows
+    // go to every rank's full Y (peer_y[r] = rank r's Y + this rank's first
+    // column, row stride ldy) instead of y, each CTA then adds the number of
+    // elements it stored to every rank's arrival counter, and CTA (0,0)
+    // waits until this rank's counter reaches gather_target, so the grid
+    // completes only when this rank's full Y has arrived.
+    int32_t n_peers;
+    int32_t rank;
+    unsigned long long gather_target;
+    __nv_bfloat16* peer_y[8];
+    unsigned long long* peer_flag[8];
 };
+constexpr int kMaxPeers = 8;
 
 // Packed weight layout (TC kernel only): W cut into kPackRows-row tiles and
 // 128-byte K chunks; chunk c of tile t is one contiguous [kPackRows][128 B]
@@ -474,16 +487,45 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (!*abort_flag) {
             const int n0 = tile * TILE_M;
             const int vecs = own_cnt / 8;  // 16-byte vectors per output row
-            const bool vec = ((reinterpret_cast<uintptr_t>(p.y) & 15u) == 0) && (p.ldy % 8 == 0);
-            for (int c = threadIdx.x - 64; c < p.m * vecs; c += 128) {
-                const int m = c / vecs;
-                const int j = own_lo + (c % vecs) * 8;
-                const __nv_bfloat16* src = ystage + m * TILE_M + j;
-                __nv_bfloat16* dst = p.y + static_cast<size_t>(m) * p.ldy + n0 + j;
-                if (vec && n0 + j + 8 <= p.n) {
-                    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
-                } else {
-                    for (int e = 0; e < 8 && n0 + j + e < p.n; ++e) dst[e] = src[e];
+            // Destinations: y, or this rank's column block of every rank's
+            // full Y (peer stores over NVLink for r != rank).
+            const int ndst = p.n_peers > 0 ? p.n_peers : 1;
+            for (int d = 0; d < ndst; ++d) {
+                __nv_bfloat16* base = p.n_peers > 0 ? p.peer_y[d] : p.y;
+                const bool vec = ((reinterpret_cast<uintptr_t>(base) & 15u) == 0) && (p.ldy % 8 == 0);
+                for (int c = threadIdx.x - 64; c < p.m * vecs; c += 128) {
+                    const int m = c / vecs;
+                    const int j = own_lo + (c % vecs) * 8;
+                    const __nv_bfloat16* src = ystage + m * TILE_M + j;
+                    __nv_bfloat16* dst = base + static_cast<size_t>(m) * p.ldy + n0 + j;
+                    if (vec && n0 + j + 8 <= p.n) {
+                        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+                    } else {
+                        for (int e = 0; e < 8 && n0 + j + e < p.n; ++e) dst[e] = src[e];
+                    }
+                }
+            }
+            if (p.n_peers > 0) {
+                // Every store of this CTA (the named barrier orders them
+                // before thread 64), then one release per rank at system
+                // scope: its counter grows by the elements this CTA wrote.
+                epilogue_bar_sync();
+                if (threadIdx.x == 64) {
+                    const int cols = max(0, min(own_cnt, p.n - (n0 + own_lo)));
+                    const unsigned long long cnt = static_cast<unsigned long long>(p.m) * cols;
+                    fence_acq_rel_sys();
+                    for (int d = 0; d < p.n_peers; ++d) red_relaxed_sys_add_u64(p.peer_flag[d], cnt);
+                    if (blockIdx.x == 0 && blockIdx.y == 0) {
+                        // Bounded wait for every rank's rows of this call.
+                        const uint64_t t0 = globaltimer_ns();
+                        while (ld_acquire_sys_u64(p.peer_flag[p.rank]) < p.gather_target) {
+                            if (globaltimer_ns() - t0 > p.timeout_ns) {
+                                atomicOr(&g_err_word, kErrPeerWait);
+                                break;
+                            }
+                            __nanosleep(32);
+                        }
+                    }
                 }
             }
         }

@@ -305,6 +305,22 @@ __device__ __forceinline__ void cluster_wait_acquire() {
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// ---------------------------------------------------------------- system scope (peer GPUs)
+// Release fence at system scope, then relaxed adds: the release pattern for
+// counters that may live in another GPU's memory.
+__device__ __forceinline__ void fence_acq_rel_sys() {
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+__device__ __forceinline__ void red_relaxed_sys_add_u64(unsigned long long* addr,
+                                                        unsigned long long v) {
+    asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(addr), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* addr) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(addr) : "memory");
+    return v;
+}
+
 // ---------------------------------------------------------------- FP8 widening
 // Two E4M3 codes (low 16 bits) -> two floats, exactly, via CUDA's
 // fp8x2 -> half2 conversion intrinsic.

@@ -57,6 +57,10 @@ EXPORTED = (
     "tinym_quant_workspace_bytes",
     "tinym_fp8_gemm_quant_act",
     "tinym_fp8_gemm_quant_act_noalloc",
+    "tinym_fp8_gemm_allgather",
+    "tinym_ipc_export",
+    "tinym_ipc_open",
+    "tinym_ipc_close",
     "tinym_status_string",
     "tinym_last_error",
     "tinym_abi_version",
@@ -85,6 +89,20 @@ class Plan(ctypes.Structure):
 
     def __repr__(self) -> str:  # pragma: no cover - debugging aid
         return f"Plan({self.as_dict()})"
+
+
+class GatherDesc(ctypes.Structure):
+    """Mirror of ``tinym_gather_desc`` (include/tinym_b200.h)."""
+
+    _fields_ = [
+        ("world", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("n_full", ctypes.c_int64),
+        ("col0", ctypes.c_int64),
+        ("y_full", ctypes.c_void_p * 8),
+        ("flag", ctypes.c_void_p * 8),
+        ("target", ctypes.c_uint64),
+    ]
 
 
 class TinymError(RuntimeError):
@@ -146,6 +164,16 @@ def capi() -> ctypes.CDLL:
                                                              i64, i64, i64,
                                                              ctypes.POINTER(Plan), vp]
             lib.tinym_fp8_gemm_quant_act_noalloc.restype = ctypes.c_int
+            lib.tinym_fp8_gemm_allgather.argtypes = [vp, vp, i64, i64, i64, vp, f32,
+                                                     ctypes.POINTER(GatherDesc),
+                                                     ctypes.POINTER(Plan), vp]
+            lib.tinym_fp8_gemm_allgather.restype = ctypes.c_int
+            lib.tinym_ipc_export.argtypes = [vp, vp, ctypes.POINTER(i64)]
+            lib.tinym_ipc_export.restype = ctypes.c_int
+            lib.tinym_ipc_open.argtypes = [vp, ctypes.POINTER(vp)]
+            lib.tinym_ipc_open.restype = ctypes.c_int
+            lib.tinym_ipc_close.argtypes = [vp]
+            lib.tinym_ipc_close.restype = ctypes.c_int
             lib.tinym_status_string.argtypes = [ctypes.c_int32]
             lib.tinym_status_string.restype = ctypes.c_char_p
             lib.tinym_last_error.argtypes = []
@@ -269,6 +297,36 @@ def gemm_quant_act(x, w, w_scale, *, out=None, workspace=None, plan: Plan | None
     return out, workspace
 
 
+def ipc_export(ptr: int) -> tuple[bytes, int]:
+    """CUDA IPC handle (64 bytes) of the allocation holding device pointer
+    ptr, and ptr's byte offset in that allocation."""
+    h = ctypes.create_string_buffer(64)
+    off = ctypes.c_int64(0)
+    _check(capi().tinym_ipc_export(ptr, h, ctypes.byref(off)))
+    return h.raw, int(off.value)
+
+
+def ipc_open(handle: bytes) -> int:
+    """Map a peer process's allocation into this one; returns its base."""
+    base = ctypes.c_void_p(0)
+    _check(capi().tinym_ipc_open(ctypes.create_string_buffer(handle, 64), ctypes.byref(base)))
+    return int(base.value)
+
+
+def ipc_close(base: int) -> None:
+    _check(capi().tinym_ipc_close(base))
+
+
+def gemm_allgather_ptr(x_ptr: int, w_ptr: int, m: int, n_local: int, k: int, desc: GatherDesc,
+                       *, alpha: float = 1.0, alpha_ptr: int | None = None,
+                       plan: Plan | None = None, stream: int = 0) -> None:
+    """N-sharded GEMM whose epilogue stores into every rank's full Y
+    (tinym_fp8_gemm_allgather)."""
+    pl = ctypes.byref(plan) if plan is not None else None
+    _check(capi().tinym_fp8_gemm_allgather(x_ptr, w_ptr, m, n_local, k, alpha_ptr, alpha,
+                                           ctypes.byref(desc), pl, stream))
+
+
 def max_active_clusters(m: int, n: int, k: int, plan: Plan) -> int:
     """Clusters of `plan` the current GPU can hold resident at once."""
     out = ctypes.c_int32(0)
@@ -309,5 +367,6 @@ __all__ = [
     "capi", "load_torch_op", "select_plan", "check_plan", "make_plan", "gemm_ptr", "gemm",
     "device_status", "Plan", "TinymError", "EXPORTED", "KERNEL_TC", "KERNEL_SIMT_M1",
     "packed_weight_bytes", "pack_weights_ptr", "gemm_packed_ptr", "quant_workspace_bytes",
-    "gemm_quant_act", "ACT_BF16", "ACT_F32",
+    "gemm_quant_act", "ACT_BF16", "ACT_F32", "GatherDesc", "ipc_export", "ipc_open", "ipc_close",
+    "gemm_allgather_ptr",
 ]

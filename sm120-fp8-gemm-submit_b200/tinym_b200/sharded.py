@@ -5,10 +5,13 @@ slab of N, cut at multiples of the 128-row W tile where the split allows --
 and computes Y[:, start_r:stop_r] = alpha * X . W_r^T with the single-GPU
 kernel.  X (at most 16 x K bytes) and alpha are replicated.  No reduction is
 needed (K is not split across GPUs).  Optionally the BF16 slabs are
-all-gathered over NCCL into the full Y[M, N] on every rank.
+all-gathered into the full Y[M, N] on every rank: over NCCL, or fused into
+the GEMM (``enable_fused_gather``): each rank's epilogue stores its rows
+straight into every rank's Y through CUDA IPC peer mappings over NVLink and
+signals per-rank arrival counters (tinym_fp8_gemm_allgather).
 
-The reference has no multi-GPU code; this wrapper is new (its collective is
-the only data exchange, and it moves only M*N*2 bytes).
+The reference has no multi-GPU code; this wrapper is new (its gather is the
+only data exchange, and it moves only M*N*2 bytes).
 """
 
 from __future__ import annotations
@@ -86,6 +89,92 @@ class ShardedFp8Gemm:
         if self.stop > self.start:
             self._gemm(x, alpha, out)
         return out
+
+    # ---------------------------------------------------------------- fused gather
+    def enable_fused_gather(self, m_max: int = 16, device=None):
+        """Set up the fused all-gather: two [m_max, N] BF16 buffers (used
+        alternately) and an arrival counter on this rank, exported to and
+        mapped by every rank (collective: call on all ranks)."""
+        import torch
+        import torch.distributed as dist
+
+        from . import GatherDesc, ipc_export, ipc_open
+
+        device = device or torch.device("cuda", torch.cuda.current_device())
+        world = dist.get_world_size(self.group)
+        rank = dist.get_rank(self.group)
+        if world > 8:
+            raise ValueError("the fused all-gather supports up to 8 ranks")
+        self._ybuf = torch.empty((2, m_max, self.n), dtype=torch.bfloat16, device=device)
+        self._counter = torch.zeros(1, dtype=torch.int64, device=device)
+        torch.cuda.synchronize(device)
+        mine = (ipc_export(self._ybuf.data_ptr()), ipc_export(self._counter.data_ptr()))
+        allh = [None] * world
+        dist.all_gather_object(allh, mine, group=self.group)
+        self._opened = []
+        y_ptr, c_ptr = [], []
+        for r, ((hy, oy), (hc, oc)) in enumerate(allh):
+            if r == rank:
+                y_ptr.append(self._ybuf.data_ptr())
+                c_ptr.append(self._counter.data_ptr())
+                continue
+            by = ipc_open(hy)
+            self._opened.append(by)
+            bc = by if hc == hy else ipc_open(hc)
+            if bc != by:
+                self._opened.append(bc)
+            y_ptr.append(by + oy)
+            c_ptr.append(bc + oc)
+        self._m_max, self._y_ptr, self._c_ptr = m_max, y_ptr, c_ptr
+        self._epoch = 0
+        self._arrived = 0  # running sum of M * N over the fused calls so far
+        self._world, self._rank = world, rank
+        self._desc = GatherDesc()
+        self._desc.world, self._desc.rank = world, rank
+        self._desc.n_full, self._desc.col0 = self.n, self.start
+        for r in range(world):
+            self._desc.flag[r] = c_ptr[r]
+        dist.barrier(group=self.group)
+
+    def fused(self, x, alpha):
+        """Y[M, N] on every rank with the gather fused into the GEMM.  The
+        result is a view of an internal buffer that stays valid until the
+        call after next (two buffers alternate)."""
+        import torch
+
+        from . import gemm_allgather_ptr
+
+        m, k = int(x.shape[0]), int(x.shape[1])
+        if m > self._m_max:
+            raise ValueError(f"M={m} > m_max={self._m_max}")
+        self._epoch += 1
+        buf = self._epoch & 1
+        plane = self._m_max * self.n * 2  # bytes of one [m_max, N] BF16 buffer
+        for r in range(self._world):
+            self._desc.y_full[r] = self._y_ptr[r] + buf * plane
+        self._arrived += m * self.n
+        self._desc.target = self._arrived
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        if isinstance(alpha, torch.Tensor):
+            gemm_allgather_ptr(x.data_ptr(), self.w_local.data_ptr(), m, self.stop - self.start,
+                               k, self._desc, alpha_ptr=alpha.data_ptr(), stream=stream)
+        else:
+            gemm_allgather_ptr(x.data_ptr(), self.w_local.data_ptr(), m, self.stop - self.start,
+                               k, self._desc, alpha=float(alpha), stream=stream)
+        return self._ybuf[buf, :m]
+
+    def close_fused_gather(self):
+        """Unmap the peers' buffers (collective: call on all ranks)."""
+        import torch
+        import torch.distributed as dist
+
+        from . import ipc_close
+
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for base in getattr(self, "_opened", []):
+            ipc_close(base)
+        self._opened = []
 
     def __call__(self, x, alpha, gather: bool = True):
         """Y[M, N] on every rank (gather=True) or this rank's slab."""

@@ -33,7 +33,7 @@ def test_library_exports_every_declared_symbol():
     lib = tinym_b200.capi()
     for name in declared_symbols():
         assert hasattr(lib, name), name
-    assert lib.tinym_abi_version() == 4
+    assert lib.tinym_abi_version() == 5
 
 
 def test_status_strings():
@@ -220,3 +220,25 @@ def test_packed_weight_bytes():
     assert t.packed_weight_bytes(300, 1152) == 3 * 12 * 128 * 128
     with pytest.raises(t.TinymError):
         t.packed_weight_bytes(4, 24)  # K % 16 != 0
+
+
+def test_gather_descriptor_layout_and_host_checks():
+    """tinym_gather_desc mirrors the header, and a bad descriptor is refused
+    before any CUDA call."""
+    import tinym_b200 as t
+
+    assert ctypes.sizeof(t.GatherDesc) == 4 + 4 + 8 + 8 + 64 + 64 + 8
+    lib = t.capi()
+    d = t.GatherDesc()
+    d.world, d.rank, d.n_full, d.col0 = 0, 0, 128, 0
+    assert lib.tinym_fp8_gemm_allgather(16, 16, 1, 128, 128, None, 1.0, ctypes.byref(d),
+                                        None, None) == 1
+    d.world, d.rank = 2, 0
+    d.y_full[0] = d.y_full[1] = 256
+    d.flag[0], d.flag[1] = 512, 516  # second counter not 8-byte aligned
+    assert lib.tinym_fp8_gemm_allgather(16, 16, 1, 128, 128, None, 1.0, ctypes.byref(d),
+                                        None, None) == 1
+    d.flag[1] = 520
+    d.col0 = 64  # 64 + 128 > N_full
+    assert lib.tinym_fp8_gemm_allgather(16, 16, 1, 128, 128, None, 1.0, ctypes.byref(d),
+                                        None, None) == 1

@@ -44,6 +44,14 @@ import time
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
+
+# stdout carries exactly one JSON line: NCCL's version banner (all that
+# NCCL_DEBUG=VERSION prints) is switched off, and any other NCCL log level
+# goes to stderr.  Set before torch (and NCCL) is loaded.
+if os.environ.get("NCCL_DEBUG", "").upper() == "VERSION":
+    os.environ["NCCL_DEBUG"] = "NONE"
+if os.environ.get("NCCL_DEBUG"):
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
 sys.path.insert(0, str(ROOT))
 sys.path.insert(0, str(ROOT / "sm120-fp8-gemm-submit_b200"))
 
@@ -320,9 +328,6 @@ def main():
 
         import torch.distributed as dist
 
-        # NCCL's log (its version banner included) goes to stderr, so stdout
-        # carries only the bench line.
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=device)
 

@@ -69,7 +69,7 @@ def _worker(rank, world, port, shapes, errq):
         raise
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4])
 def test_fused_allgather_matches_slab_gemms(world):
     import torch
     import torch.multiprocessing as mp

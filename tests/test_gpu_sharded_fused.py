@@ -95,3 +95,67 @@ def test_fused_allgather_matches_slab_gemms(world):
         errs.append(errq.get())
     assert not alive, "a rank did not finish"
     assert not errs and all(p.exitcode == 0 for p in procs), errs
+
+
+def _single_rank_desc(y_full, counter, m, n, target):
+    import tinym_b200
+
+    d = tinym_b200.GatherDesc()
+    d.world, d.rank, d.n_full, d.col0 = 1, 0, n, 0
+    d.y_full[0] = y_full.data_ptr()
+    d.flag[0] = counter.data_ptr()
+    d.target = target
+    return d
+
+
+def test_fused_gather_epilogue_single_rank(cuda_device, oracle):
+    """World size 1: the fused-gather epilogue (store into the full Y, count,
+    wait) gives the plain GEMM's bits, call after call."""
+    import torch
+
+    import tinym_b200
+
+    k, n = 2048, 1000
+    _, wq, _, _, _ = oracle.make_case(1, k, n, seed=9, dist="normal")
+    w = torch.from_numpy(wq).to(cuda_device).view(torch.float8_e4m3fn)
+    y_full = torch.empty((16, n), dtype=torch.bfloat16, device=cuda_device)
+    counter = torch.zeros(1, dtype=torch.int64, device=cuda_device)
+    total = 0
+    for call, m in enumerate((1, 9, 16, 4)):
+        xq, _, _, _, alpha = oracle.make_case(m, k, 1, seed=call, dist="normal")
+        x = torch.from_numpy(xq).to(cuda_device).view(torch.float8_e4m3fn)
+        a = torch.from_numpy(alpha).to(cuda_device)
+        total += m * n
+        d = _single_rank_desc(y_full, counter, m, n, total)
+        tinym_b200.gemm_allgather_ptr(x.data_ptr(), w.data_ptr(), m, n, k, d,
+                                      alpha_ptr=a.data_ptr(),
+                                      stream=torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert torch.equal(y_full[:m], tinym_b200.gemm(x, w, a))
+        assert int(counter.item()) == total
+    assert tinym_b200.device_status() == 0
+
+
+def test_fused_gather_wait_timeout_reports(cuda_device, oracle):
+    """A counter that never reaches its target: the GEMM's bounded wait gives
+    up (1 s), sets bit 0x40 of the device error word and the context stays
+    usable (no fault, no hang)."""
+    import torch
+
+    import tinym_b200
+
+    k, n, m = 1024, 512, 9
+    xq, wq, _, _, alpha = oracle.make_case(m, k, n, seed=4, dist="normal")
+    x = torch.from_numpy(xq).to(cuda_device).view(torch.float8_e4m3fn)
+    w = torch.from_numpy(wq).to(cuda_device).view(torch.float8_e4m3fn)
+    a = torch.from_numpy(alpha).to(cuda_device)
+    y_full = torch.empty((m, n), dtype=torch.bfloat16, device=cuda_device)
+    counter = torch.zeros(1, dtype=torch.int64, device=cuda_device)
+    d = _single_rank_desc(y_full, counter, m, n, m * n + 1)  # one element never arrives
+    tinym_b200.gemm_allgather_ptr(x.data_ptr(), w.data_ptr(), m, n, k, d,
+                                  alpha_ptr=a.data_ptr(),
+                                  stream=torch.cuda.current_stream().cuda_stream)
+    assert tinym_b200.device_status() & 0x40
+    assert tinym_b200.device_status() == 0  # read-and-clear
+    assert torch.equal(y_full, tinym_b200.gemm(x, w, a))  # the rows themselves were stored
+    assert tinym_b200.device_status() == 0

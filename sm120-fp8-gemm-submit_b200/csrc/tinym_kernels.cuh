@@ -12,11 +12,13 @@
 //
 // Two consumers share this skeleton:
 //
-//  * tinym_tc_kernel<MMA_N> ("swap-AB"): the W tile [128 x 128 B] is the A
-//    operand of tcgen05.mma.kind::f8f6f4 (MMA M = 128) and X, padded by TMA
-//    zero fill to MMA_N (8 or 16) rows, is the B operand.  The accumulator
-//    D[128 x MMA_N] (FP32) lives in tensor memory; four epilogue warps read
-//    it with tcgen05.ld.  Replaces the reference's M<=16 mma.sync kernel
+//  * tinym_tc_kernel<MMA_N, CHUNKS, TILE_M> ("swap-AB"): the W tile
+//    [TILE_M x 128 B] is the A operand of tcgen05.mma.kind::f8f6f4 (MMA M =
+//    TILE_M = 128, or 64) and X, padded by TMA zero fill to MMA_N (8 or 16)
+//    rows, is the B operand.  The accumulator D[TILE_M x MMA_N] (FP32) lives
+//    in tensor memory; four epilogue warps read it with tcgen05.ld, scale it,
+//    convert it to BF16 and store it -- to Y, or (fused all-gather) to every
+//    rank's Y over NVLink.  Replaces the reference's M<=16 mma.sync kernel
 //    (include/fp8_gemm_tinym.cuh:321-461), whose m16n8k32 warp MMA put M on
 //    the MMA's M side.
 //
@@ -26,11 +28,12 @@
 //    warp shuffles.  The M=1 counterpart of the reference's scalar kernel
 //    (include/fp8_gemm_tinym.cuh:521-722).
 //
-// Both stream W with 2-D TMA boxes of 128 rows x 128 bytes using the
-// 128-byte swizzle into a ring of `stages` shared-memory slots guarded by
-// full/empty mbarriers.  Every wait is bounded (WaitGuard): a wait that runs
-// out sets a bit in the device error word and the CTA drains what it has in
-// flight, frees its tensor memory and exits.
+// Both stream W with TMA into a ring of `stages` shared-memory slots guarded
+// by full/empty mbarriers, using the 128-byte swizzle: one stage is CHUNKS
+// K chunks of [TILE_M rows x 128 B], fetched by one 3-D box when CHUNKS > 1
+// (2-D boxes of 128 rows x 128 B for the SIMT kernel).  Every wait is bounded
+// (WaitGuard): a wait that runs out sets a bit in the device error word and
+// the CTA drains what it has in flight, frees its tensor memory and exits.
 #pragma once
 
 #include "tinym_ptx.cuh"

@@ -86,6 +86,7 @@ __global__ void __cluster_dims__(kQuantCtas, 1, 1) __launch_bounds__(kQuantThrea
     using V = ActVec<T>;
     __shared__ float s_warp[kQuantThreads / 32];
     __shared__ float s_amax;  // this CTA's max |x|, read by the whole cluster
+    __shared__ float s_gmax;  // the cluster's max |x|
 
     const int64_t nvec = count / V::N;  // count % V::N == 0 (K % 16 == 0)
     const uint32_t rank = cluster_ctarank();
@@ -129,9 +130,18 @@ __global__ void __cluster_dims__(kQuantCtas, 1, 1) __launch_bounds__(kQuantThrea
     // Every CTA's local maximum is published before anyone reads it ...
     cluster_arrive_release();
     cluster_wait_acquire();
-    float amax = 0.0f;
-    for (uint32_t r = 0; r < kQuantCtas; ++r)
-        amax = nan_amax(amax, dsmem_ld_f32(dsmem_map(smem_u32(&s_amax), r)));
+    // Lane r of warp 0 reads rank r's maximum (one remote latency in all),
+    // the warp combines them, and the CTA takes the result from s_gmax.
+    if (threadIdx.x < 32) {
+        float a = threadIdx.x < kQuantCtas
+                      ? dsmem_ld_f32(dsmem_map(smem_u32(&s_amax), threadIdx.x))
+                      : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a = nan_amax(a, __shfl_xor_sync(0xFFFFFFFFu, a, o));
+        if (threadIdx.x == 0) s_gmax = a;
+    }
+    __syncthreads();
+    const float amax = s_gmax;
     // ... and no CTA leaves while another may still read its s_amax.
     cluster_arrive_relaxed();
 

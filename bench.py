@@ -404,6 +404,7 @@ def main():
     # all-gather after the GEMM, and the gather fused into the GEMM's
     # epilogue (peer stores + arrival counters, tinym_fp8_gemm_allgather).
     gather_cmp = None
+    e2e_dist = None
     if dist is not None and not args.no_fused_gather:
         from tinym_b200.sharded import ShardedFp8Gemm
 
@@ -444,10 +445,51 @@ def main():
                 g.fused(sets[i % n_sets][0], sets[i % n_sets][5])
 
             gather_cmp["gemm_fused_allgather_us"] = round(device_time(fused_step), 3)
-            err_word = tinym_b200.device_status()
-            g.close_fused_gather()
+            # every rank takes the same branch: the error word's max over ranks
+            ew = torch.tensor([tinym_b200.device_status()], device=device, dtype=torch.int64)
+            dist.all_reduce(ew, op=dist.ReduceOp.MAX)
+            err_word = int(ew.item())
             if err_word:
                 gather_cmp["error"] = f"device error word 0x{err_word:x}"
+            elif args.e2e_steps > 0:
+                # End to end at N GPUs through the public API: every step each
+                # rank copies its X and W slab from pinned host memory, runs
+                # the sharded GEMM with the fused gather, and reads the full
+                # Y back to the host.
+                x0, w0, _, _, _, a0 = sets[0]
+                hx = x0.view(torch.uint8).cpu().pin_memory()
+                hw = w0.view(torch.uint8).cpu().pin_memory()
+                hy = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
+                dx = torch.empty_like(x0.view(torch.uint8))
+                dw = torch.empty_like(w0.view(torch.uint8))
+                g.w_local = dw.view(torch.float8_e4m3fn)
+
+                def e2e_dist_step():
+                    dx.copy_(hx, non_blocking=True)
+                    dw.copy_(hw, non_blocking=True)
+                    yy = g.fused(dx.view(torch.float8_e4m3fn), a0)
+                    hy.copy_(yy, non_blocking=True)
+
+                for _ in range(3):
+                    e2e_dist_step()
+                torch.cuda.synchronize()
+                dist.barrier()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(args.e2e_steps):
+                    e2e_dist_step()
+                e1.record()
+                torch.cuda.synchronize()
+                tt = torch.tensor([e0.elapsed_time(e1) / args.e2e_steps], device=device,
+                                  dtype=torch.float64)
+                dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+                e2e_ms = float(tt.item())
+                e2e_dist = {"value": round(algo_bytes(m, k, n) / (e2e_ms * 1e-3) / 1e9, 3),
+                            "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
+                            "h2d_bytes_per_step": int(hx.numel() + hw.numel()),
+                            "d2h_bytes_per_step": int(hy.numel() * 2),
+                            "api": "tinym_b200.sharded.ShardedFp8Gemm.fused (per rank; max over ranks)"}
+            g.close_fused_gather()
         except Exception as e:  # reported, not fatal to the main measurement
             gather_cmp["error"] = f"{type(e).__name__}: {e}"
 
@@ -491,6 +533,8 @@ def main():
             out["allgather_us"] = round(allgather_us, 2)
         if gather_cmp is not None:
             out["gather_of_y"] = gather_cmp
+        if e2e_dist is not None:
+            out["e2e"] = e2e_dist
 
     # ---- cuBLASLt competitor (1 GPU only, same buffers / protocol)
     if rank == 0 and world == 1 and not args.no_cublas:

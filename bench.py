@@ -372,6 +372,21 @@ def main():
     if err:
         raise SystemExit(f"device error word 0x{err:x} after the timed loop")
 
+    # the same back-to-back loop with TINYM_FLAG_STATIC_W (weights never
+    # written by the preceding kernel: W streams during the previous GEMM's
+    # tail); reported beside `value`, which stays the default behaviour
+    def ours_static(s, stream_handle):
+        x, w, y, sx, sw, alpha = s
+        tinym_b200.gemm_ptr(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n_local, k,
+                            alpha_ptr=alpha.data_ptr(), stream=stream_handle, static_w=True)
+
+    sw_steps = min(args.steps, 20000)
+    static_span = graph_throughput(ours_static, sets, sw_steps, args.warmup)
+    st_t = torch.tensor([static_span / sw_steps], device=device, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(st_t, op=dist.ReduceOp.MAX)
+    static_us = float(st_t.item()) * 1e3
+
     span_t = torch.tensor([span], device=device, dtype=torch.float64)
     if dist is not None:
         dist.all_reduce(span_t, op=dist.ReduceOp.MAX)
@@ -519,6 +534,7 @@ def main():
             "latency_protocol": f"{lat_n} single launches, each after a GPU spin spacer, "
                                 "rotating buffers (cold W), CUDA events",
             "graph_us_per_launch": round(mean_us, 3),
+            "graph_us_per_launch_static_w": round(static_us, 3),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_source": f"{peak_note} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",

@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define TINYM_ABI_VERSION 5
+#define TINYM_ABI_VERSION 6
 
 /* Exported-symbol marker (the library is built with hidden visibility). */
 #if defined(__GNUC__)
@@ -106,6 +106,27 @@ TINYM_API int tinym_fp8_gemm_ex(const void* x, const void* w, void* y, int64_t l
                       int64_t m, int64_t n, int64_t k,
                       const float* alpha_dev, float alpha,
                       const tinym_plan* plan, void* stream);
+
+/* tinym_fp8_gemm_ex with behaviour flags (TINYM_FLAG_*).
+ *
+ * TINYM_FLAG_STATIC_W: the caller guarantees that the kernel queued just
+ * before this GEMM on the stream does not write W (the usual case for
+ * inference weights).  The GEMM then starts streaming W as soon as its CTAs
+ * are resident -- under programmatic dependent launch that is during the
+ * previous kernel's tail -- and waits for the previous kernel only before
+ * it reads X and alpha and writes Y.  Without the flag nothing is read
+ * before the previous kernel has completed.  When plan is NULL the dispatch
+ * then also packs two CTAs per SM (a 64 KiB ring each, twice the K split),
+ * so consecutive GEMMs overlap. */
+#define TINYM_FLAG_STATIC_W 1u
+
+/* The plan tinym_fp8_gemm_ex2 would use with these flags (host-only). */
+TINYM_API int tinym_select_plan_ex(int64_t m, int64_t n, int64_t k, int32_t sm_count,
+                                   uint32_t flags, tinym_plan* out);
+TINYM_API int tinym_fp8_gemm_ex2(const void* x, const void* w, void* y, int64_t ldy,
+                                 int64_t m, int64_t n, int64_t k,
+                                 const float* alpha_dev, float alpha,
+                                 const tinym_plan* plan, uint32_t flags, void* stream);
 
 /* The shape-dispatch table: fills *out with the plan tinym_fp8_gemm would
  * use for (m, n, k) on a GPU with sm_count SMs.  Host-only logic (needs no

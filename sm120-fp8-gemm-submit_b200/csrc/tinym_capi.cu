@@ -329,14 +329,24 @@ int max_stages_fitting(const tinym_plan& p, uint32_t limit) {
 // best on B200 -- deeper rings (192 KiB) lose in the single-launch protocols
 // without gaining back-to-back throughput.
 constexpr int kTargetRingBytes = 128 * 1024;
+// Host-only flag bit (above the kernel's TinymParams::flags): the GEMM
+// follows the quantise prologue, which keeps the default plan.
+constexpr uint32_t kFlagQuantPrologue = 1u << 16;
+// With TINYM_FLAG_STATIC_W the dispatch instead cuts the work into twice as
+// many CTAs with a 64 KiB ring each (small enough for two per SM), so that
+// the next GEMM's CTAs take over SMs as the previous GEMM's finish and
+// stream W during its tail: measured 4-9 % more back-to-back throughput at
+// M = 9 on the official points.
+constexpr int kOverlapRingBytes = 64 * 1024;
+constexpr uint32_t kHalfSmSmem = (233472u - 2u * 1024u) / 2u;  // two CTAs' share of an SM
 
-// Ring depth for a TC plan: kTargetRingBytes of W in flight, at most what
-// fits and at most the CTA's K blocks (more is useless), at least 2; -1 if
-// not even two stages fit.
-int tc_stages_for(const tinym_plan& p, int64_t kb_per_cta) {
+// Ring depth for a TC plan: ring_bytes of W in flight, at most what fits
+// and at most the CTA's K blocks (more is useless), at least 2; -1 if not
+// even two stages fit.
+int tc_stages_for(const tinym_plan& p, int64_t kb_per_cta, int ring_bytes = kTargetRingBytes) {
     const int max_st = max_stages_fitting(p, static_cast<uint32_t>(kSmemLimit));
     if (max_st < 0) return -1;
-    const int64_t want = std::max(2, kTargetRingBytes / w_stage_bytes(p));
+    const int64_t want = std::max(2, ring_bytes / w_stage_bytes(p));
     return static_cast<int>(std::max<int64_t>(2, std::min<int64_t>({kb_per_cta, want, max_st})));
 }
 
@@ -354,25 +364,33 @@ int tc_stages_for(const tinym_plan& p, int64_t kb_per_cta) {
 //  * the largest K split (cluster size <= 8) that keeps tiles * split CTAs
 //    within one CTA per SM and gives every CTA >= 2 stages;
 //  * a ring of ~128 KiB of W (tc_stages_for).
-tinym_plan heuristic_plan(int64_t m, int64_t n, int64_t k, int sm_count) {
+// overlap = true: the TINYM_FLAG_STATIC_W variant (two CTAs per SM).
+tinym_plan heuristic_plan(int64_t m, int64_t n, int64_t k, int sm_count, bool overlap = false) {
     tinym_plan p{};
     p.kernel = TINYM_KERNEL_TC;
     p.mma_n = m <= 8 ? 8 : 16;
     p.block_k = (k % kBlockK == 0) ? 2 * kBlockK : kBlockK;
     p.split_k = 1;
     p.tile_m = kTileRows;
+    const int ring = overlap ? kOverlapRingBytes : kTargetRingBytes;
+    const int64_t slots = static_cast<int64_t>(sm_count) * (overlap ? 2 : 1);
     const int64_t tiles = (n + p.tile_m - 1) / p.tile_m;
     const int64_t kb = (k + p.block_k - 1) / p.block_k;
     for (int s = 2; s <= kMaxSplit; ++s) {
-        if (tiles * s > sm_count) break;
+        if (tiles * s > slots) break;
         const int64_t per = (kb + s - 1) / s;
         if (per < 2 || (s - 1) * per >= kb) continue;
         tinym_plan q = p;
         q.split_k = s;
-        if (tc_stages_for(q, per) < 0) continue;
+        const int st = tc_stages_for(q, per, ring);
+        if (st < 0) continue;
+        if (overlap) {
+            q.stages = st;
+            if (plan_smem_bytes(q) > kHalfSmSmem) continue;
+        }
         p.split_k = s;
     }
-    p.stages = tc_stages_for(p, (kb + p.split_k - 1) / p.split_k);
+    p.stages = tc_stages_for(p, (kb + p.split_k - 1) / p.split_k, ring);
     return p;
 }
 
@@ -402,6 +420,13 @@ int kernel_for(const tinym_plan& p, DeviceInfo* di, const void** fn) {
     if (!(di->attr_done.load(std::memory_order_acquire) & attr_bit)) {
         cudaError_t e = cudaFuncSetAttribute(*fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
+        // The whole L1/shared array as shared memory.  Plans above half an SM
+        // get this carveout at launch anyway; stating it makes the occupancy
+        // calculator (the launcher's residency check) count two CTAs per SM
+        // for plans that fit twice instead of assuming the default carveout.
+        e = cudaFuncSetAttribute(*fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 cudaSharedmemCarveoutMaxShared);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(PreferredSharedMemoryCarveout)");
         if (p.split_k > kMaxSplit) {
             e = cudaFuncSetAttribute(*fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
             if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(NonPortableClusterSize)");
@@ -569,17 +594,23 @@ static int gemm_impl(const void* x, const void* w, void* y, int64_t ldy, int64_t
         p = *plan;
         if ((st = fill_derived(m, n, k, &p)) != TINYM_OK) return st;
     } else {
-        if ((st = tinym_select_plan(m, n, k, di->sm_count, &p)) != TINYM_OK) return st;
-        // The table assumes every cluster of the grid is resident at once;
-        // shrink the K split until the device confirms that it is.
-        while (p.split_k > 1) {
+        const bool overlap = (flags & tinym::kFlagEarlyW) && !(flags & kFlagQuantPrologue);
+        p = heuristic_plan(m, n, k, di->sm_count, overlap);
+        if ((st = fill_derived(m, n, k, &p)) != TINYM_OK) return st;
+        const int ring = overlap ? kOverlapRingBytes : kTargetRingBytes;
+        // The default table assumes every cluster of the grid is resident at
+        // once; shrink the K split until the device confirms that it is.  The
+        // static-W plan is built to stream more, smaller CTAs than fit one
+        // wave (clusters are independent, so that is correct) and is left
+        // as chosen: measured faster than any shrunken variant.
+        while (!overlap && p.split_k > 1) {
             int clusters = 0;
             if ((st = max_active_clusters(p, dev, di, &clusters)) != TINYM_OK) return st;
             if (clusters >= p.tiles_n) break;
             --p.split_k;
             const int64_t kb = (k + p.block_k - 1) / p.block_k;
             const int s2 = p.kernel == TINYM_KERNEL_TC
-                               ? tc_stages_for(p, (kb + p.split_k - 1) / p.split_k)
+                               ? tc_stages_for(p, (kb + p.split_k - 1) / p.split_k, ring)
                                : p.stages;
             if (s2 > 0) p.stages = s2;
             if ((st = fill_derived(m, n, k, &p)) != TINYM_OK) return st;
@@ -612,7 +643,7 @@ static int gemm_impl(const void* x, const void* w, void* y, int64_t ldy, int64_t
     prm.kb_per_split = (prm.kb_total + p.split_k - 1) / p.split_k;
     prm.split = p.split_k;
     prm.stages = p.stages;
-    prm.flags = flags;
+    prm.flags = flags & 0xFFFFu;  // the kernel's kFlag* bits only
     prm.timeout_ns = timeout_ns;
     prm.w_packed_kc = w_packed ? static_cast<int32_t>(tinym::packed_chunks(k)) : 0;
     if (gd) {
@@ -648,6 +679,30 @@ int tinym_fp8_gemm_ex(const void* x, const void* w, void* y, int64_t ldy, int64_
                       int64_t k, const float* alpha_dev, float alpha, const tinym_plan* plan,
                       void* stream) {
     return gemm_impl(x, w, y, ldy, m, n, k, alpha_dev, alpha, plan, stream, 0u,
+                     kDefaultTimeoutNs);
+}
+
+int tinym_select_plan_ex(int64_t m, int64_t n, int64_t k, int32_t sm_count, uint32_t flags,
+                         tinym_plan* out) {
+    t_last_error[0] = '\0';
+    if (!out) return fail(TINYM_ERR_INVALID_ARGUMENT, "out is NULL");
+    if (sm_count < 1) return fail(TINYM_ERR_INVALID_ARGUMENT, "sm_count must be positive");
+    if (flags & ~static_cast<uint32_t>(TINYM_FLAG_STATIC_W))
+        return fail(TINYM_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
+    int st = check_shape(m, n, k);
+    if (st != TINYM_OK) return st;
+    *out = heuristic_plan(m, n, k, sm_count, (flags & TINYM_FLAG_STATIC_W) != 0);
+    return fill_derived(m, n, k, out);
+}
+
+int tinym_fp8_gemm_ex2(const void* x, const void* w, void* y, int64_t ldy, int64_t m, int64_t n,
+                       int64_t k, const float* alpha_dev, float alpha, const tinym_plan* plan,
+                       uint32_t flags, void* stream) {
+    t_last_error[0] = '\0';
+    if (flags & ~static_cast<uint32_t>(TINYM_FLAG_STATIC_W))
+        return fail(TINYM_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
+    const uint32_t kflags = (flags & TINYM_FLAG_STATIC_W) ? tinym::kFlagEarlyW : 0u;
+    return gemm_impl(x, w, y, ldy, m, n, k, alpha_dev, alpha, plan, stream, kflags,
                      kDefaultTimeoutNs);
 }
 
@@ -697,7 +752,7 @@ int tinym_fp8_gemm_quant_act(const void* x_act, int32_t act_dtype, const void* w
     if (e != cudaSuccess) return cuda_fail(e, "quantise kernel launch");
     return gemm_impl(ws + tinym::kQuantWsHeader, w, y, ldy, m, n, k,
                      reinterpret_cast<const float*>(ws) + 1, 0.0f, plan, stream,
-                     tinym::kFlagEarlyW, kDefaultTimeoutNs);
+                     tinym::kFlagEarlyW | kFlagQuantPrologue, kDefaultTimeoutNs);
 }
 
 int tinym_fp8_gemm_quant_act_noalloc(const void* x_act, int32_t act_dtype, const void* w,

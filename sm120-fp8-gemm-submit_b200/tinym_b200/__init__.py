@@ -46,6 +46,8 @@ EXPORTED = (
     "tinym_fp8_gemm",
     "tinym_fp8_gemm_dev_alpha",
     "tinym_fp8_gemm_ex",
+    "tinym_fp8_gemm_ex2",
+    "tinym_select_plan_ex",
     "tinym_select_plan",
     "tinym_check_plan",
     "tinym_device_status",
@@ -136,6 +138,12 @@ def capi() -> ctypes.CDLL:
             lib.tinym_fp8_gemm_ex.argtypes = [vp, vp, vp, i64, i64, i64, i64, vp, f32,
                                               ctypes.POINTER(Plan), vp]
             lib.tinym_fp8_gemm_ex.restype = ctypes.c_int
+            lib.tinym_fp8_gemm_ex2.argtypes = [vp, vp, vp, i64, i64, i64, i64, vp, f32,
+                                               ctypes.POINTER(Plan), ctypes.c_uint32, vp]
+            lib.tinym_fp8_gemm_ex2.restype = ctypes.c_int
+            lib.tinym_select_plan_ex.argtypes = [i64, i64, i64, ctypes.c_int32, ctypes.c_uint32,
+                                                 ctypes.POINTER(Plan)]
+            lib.tinym_select_plan_ex.restype = ctypes.c_int
             lib.tinym_select_plan.argtypes = [i64, i64, i64, ctypes.c_int32, ctypes.POINTER(Plan)]
             lib.tinym_select_plan.restype = ctypes.c_int
             lib.tinym_check_plan.argtypes = [i64, i64, i64, ctypes.POINTER(Plan)]
@@ -205,10 +213,14 @@ def load_torch_op() -> None:
             _torch_op_loaded = True
 
 
-def select_plan(m: int, n: int, k: int, sm_count: int = 148) -> Plan:
-    """The shape-dispatch table's choice for (m, n, k) on sm_count SMs."""
+def select_plan(m: int, n: int, k: int, sm_count: int = 148, static_w: bool = False) -> Plan:
+    """The shape-dispatch table's choice for (m, n, k) on sm_count SMs
+    (with TINYM_FLAG_STATIC_W's two-CTA-per-SM variant when static_w)."""
     p = Plan()
-    _check(capi().tinym_select_plan(m, n, k, sm_count, ctypes.byref(p)))
+    if static_w:
+        _check(capi().tinym_select_plan_ex(m, n, k, sm_count, 1, ctypes.byref(p)))
+    else:
+        _check(capi().tinym_select_plan(m, n, k, sm_count, ctypes.byref(p)))
     return p
 
 
@@ -228,14 +240,22 @@ def make_plan(kernel: int = KERNEL_TC, split_k: int = 1, stages: int = 4, mma_n:
     return p
 
 
+FLAG_STATIC_W = 1
+
+
 def gemm_ptr(x_ptr: int, w_ptr: int, y_ptr: int, m: int, n: int, k: int, *,
              ldy: int | None = None, alpha: float = 1.0, alpha_ptr: int | None = None,
-             plan: Plan | None = None, stream: int = 0) -> None:
-    """Y = alpha * X . W^T through tinym_fp8_gemm_ex on raw device pointers."""
+             plan: Plan | None = None, stream: int = 0, static_w: bool = False) -> None:
+    """Y = alpha * X . W^T through tinym_fp8_gemm_ex on raw device pointers
+    (tinym_fp8_gemm_ex2 with TINYM_FLAG_STATIC_W when static_w)."""
     lib = capi()
     pl = ctypes.byref(plan) if plan is not None else None
-    st = lib.tinym_fp8_gemm_ex(x_ptr, w_ptr, y_ptr, n if ldy is None else ldy, m, n, k,
-                               alpha_ptr, alpha, pl, stream)
+    if static_w:
+        st = lib.tinym_fp8_gemm_ex2(x_ptr, w_ptr, y_ptr, n if ldy is None else ldy, m, n, k,
+                                    alpha_ptr, alpha, pl, FLAG_STATIC_W, stream)
+    else:
+        st = lib.tinym_fp8_gemm_ex(x_ptr, w_ptr, y_ptr, n if ldy is None else ldy, m, n, k,
+                                   alpha_ptr, alpha, pl, stream)
     _check(st)
 
 
@@ -343,7 +363,7 @@ def device_status(clear: bool = True) -> int:
     return int(flags.value)
 
 
-def gemm(x, w, alpha, *, out=None, plan: Plan | None = None):
+def gemm(x, w, alpha, *, out=None, plan: Plan | None = None, static_w: bool = False):
     """torch convenience wrapper over the C ABI (device alpha, current stream)."""
     import torch
 
@@ -356,10 +376,10 @@ def gemm(x, w, alpha, *, out=None, plan: Plan | None = None):
     stream = torch.cuda.current_stream(x.device).cuda_stream
     if isinstance(alpha, torch.Tensor):
         gemm_ptr(x.data_ptr(), w.data_ptr(), out.data_ptr(), m, n, k, ldy=out.stride(0),
-                 alpha_ptr=alpha.data_ptr(), plan=plan, stream=stream)
+                 alpha_ptr=alpha.data_ptr(), plan=plan, stream=stream, static_w=static_w)
     else:
         gemm_ptr(x.data_ptr(), w.data_ptr(), out.data_ptr(), m, n, k, ldy=out.stride(0),
-                 alpha=float(alpha), plan=plan, stream=stream)
+                 alpha=float(alpha), plan=plan, stream=stream, static_w=static_w)
     return out
 
 

@@ -33,7 +33,7 @@ def test_library_exports_every_declared_symbol():
     lib = tinym_b200.capi()
     for name in declared_symbols():
         assert hasattr(lib, name), name
-    assert lib.tinym_abi_version() == 5
+    assert lib.tinym_abi_version() == 6
 
 
 def test_status_strings():
@@ -242,3 +242,19 @@ def test_gather_descriptor_layout_and_host_checks():
     d.col0 = 64  # 64 + 128 > N_full
     assert lib.tinym_fp8_gemm_allgather(16, 16, 1, 128, 128, None, 1.0, ctypes.byref(d),
                                         None, None) == 1
+
+
+def test_static_w_dispatch_packs_two_ctas_per_sm():
+    """TINYM_FLAG_STATIC_W: 64 KiB rings (two CTAs fit an SM) and twice the K
+    split of the default table at the official points."""
+    import tinym_b200 as t
+
+    for m in (1, 9, 16):
+        for k, n, split in ((6144, 5120, 6), (5120, 8192, 4), (5120, 16384, 2)):
+            p = t.select_plan(m, n, k, 148, static_w=True)
+            assert (p.block_k, p.stages, p.split_k) == (256, 2, split), p.as_dict()
+            assert p.smem_bytes <= (233472 - 2048) // 2
+            assert p.grid_ctas <= 2 * 148
+    lib = t.capi()
+    out = t.Plan()
+    assert lib.tinym_select_plan_ex(9, 5120, 6144, 148, 4, ctypes.byref(out)) == 1  # bad flag

@@ -294,3 +294,56 @@ def test_error_paths(cuda_device, oracle):
     with pytest.raises(tinym_b200.TinymError, match="BAD_PLAN"):
         tinym_b200.gemm(torch.zeros(2, 256, device=dev).to(f8), b, 1.0, plan=bad)
     assert tinym_b200.device_status() == 0
+
+
+def test_static_w_flag_honours_x_dependency(cuda_device, oracle):
+    """TINYM_FLAG_STATIC_W streams W before the dependency wait but must still
+    read X only after the kernel that writes it: each GEMM follows a copy
+    kernel that rewrites X, back to back and inside a CUDA graph."""
+    import torch
+
+    import tinym_b200
+
+    m, k, n = 9, 6144, 5120
+    _, wq, _, _, alpha = oracle.make_case(m, k, n, seed=77, dist="normal")
+    w = _to_dev(wq, cuda_device)
+    a = torch.from_numpy(alpha).to(cuda_device)
+    xq_list = [oracle.make_case(m, k, 1, seed=300 + i, dist="normal")[0] for i in range(4)]
+    xs = [_to_dev(xq, cuda_device) for xq in xq_list]
+    # the flag changes the dispatch (more, smaller CTAs), so the bit-exact
+    # reference is the same plan run without the flag
+    plan = tinym_b200.select_plan(m, n, k, torch.cuda.get_device_properties(cuda_device)
+                                  .multi_processor_count, static_w=True)
+    refs = [tinym_b200.gemm(x, w, a, plan=plan) for x in xs]
+    for xq, r in zip(xq_list, refs):
+        _check(oracle, r, xq, wq, alpha)
+    x = torch.empty_like(xs[0])
+    y = torch.empty((m, n), dtype=torch.bfloat16, device=cuda_device)
+    for rep in range(3):
+        for i in range(4):
+            x.view(torch.uint8).copy_(xs[i].view(torch.uint8))
+            tinym_b200.gemm(x, w, a, out=y, static_w=True)
+            assert torch.equal(y, refs[i]), (rep, i)
+    # the same chain captured in a graph: copy -> GEMM, four times per replay
+    outs = [torch.empty_like(y) for _ in range(4)]
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        tinym_b200.gemm(x, w, a, out=outs[0], static_w=True)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(4):
+            x.view(torch.uint8).copy_(xs[i].view(torch.uint8))
+            tinym_b200.gemm(x, w, a, out=outs[i], static_w=True)
+    for _ in range(3):
+        for o in outs:
+            o.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        for i in range(4):
+            assert torch.equal(outs[i], refs[i])
+    assert tinym_b200.device_status() == 0
+    lib = tinym_b200.capi()
+    assert lib.tinym_fp8_gemm_ex2(x.data_ptr(), w.data_ptr(), y.data_ptr(), n, m, n, k,
+                                  a.data_ptr(), 0.0, None, 2, None) == 1  # unknown flag

@@ -258,3 +258,57 @@ def test_static_w_dispatch_packs_two_ctas_per_sm():
     lib = t.capi()
     out = t.Plan()
     assert lib.tinym_select_plan_ex(9, 5120, 6144, 148, 4, ctypes.byref(out)) == 1  # bad flag
+
+
+def test_quant_act_host_checks():
+    """Workspace size and the fused activation path's argument checks run on
+    the host, before any CUDA call."""
+    import tinym_b200 as t
+
+    assert t.quant_workspace_bytes(9, 6144) == 256 + 55296
+    assert t.quant_workspace_bytes(1, 16) == 256 + 256  # codes rounded to 256 bytes
+    with pytest.raises(t.TinymError):
+        t.quant_workspace_bytes(17, 128)
+    lib = t.capi()
+    # null workspace, bad dtype, misaligned X, misaligned workspace: every call
+    # fails before any pointer is used
+    # (x, dtype, w, w_scale, y, ldy, m, n, k, workspace, plan, stream)
+    assert lib.tinym_fp8_gemm_quant_act(256, 1, 256, 256, 256, 128, 1, 128, 128, None, None,
+                                        None) == 1
+    assert lib.tinym_fp8_gemm_quant_act(256, 3, 256, 256, 256, 128, 1, 128, 128, 512, None,
+                                        None) == 1
+    assert lib.tinym_fp8_gemm_quant_act(264, 1, 256, 256, 256, 128, 1, 128, 128, 512, None,
+                                        None) == 3
+    assert lib.tinym_fp8_gemm_quant_act(256, 1, 256, 256, 256, 128, 1, 128, 128, 528, None,
+                                        None) == 3
+
+
+def test_ipc_export_rejects_null_arguments():
+    import tinym_b200 as t
+
+    lib = t.capi()
+    off = ctypes.c_int64(0)
+    h = ctypes.create_string_buffer(64)
+    assert lib.tinym_ipc_export(None, h, ctypes.byref(off)) == 1
+    base = ctypes.c_void_p(0)
+    assert lib.tinym_ipc_open(None, ctypes.byref(base)) == 1
+
+
+def test_bench_reference_arm_prints_one_line():
+    """The driver's reference arm: the CPU oracle on the host cores, one JSON
+    line with the contract's keys."""
+    import json
+    import subprocess
+    import sys
+
+    root = Path(__file__).resolve().parents[1]
+    res = subprocess.run([sys.executable, str(root / "bench.py"), "--impl", "reference",
+                          "--steps", "1", "--warmup", "3"],
+                         capture_output=True, text=True, timeout=240, cwd=root)
+    assert res.returncode == 0, res.stderr[-2000:]
+    lines = [ln for ln in res.stdout.strip().splitlines() if ln.strip()]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["unit"] == "GB/s" and d["value"] > 0
+    assert d["cpu_baseline"]["kind"] in ("port", "reference")
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["gpu_launches"] == 0

@@ -243,6 +243,50 @@ def graph_throughput(fn, sets, steps, warmup):
     return e0.elapsed_time(e1)
 
 
+def gpu_local_cpus(device_index):
+    """CPUs on the GPU's NUMA side (NVML's CPU affinity of the device, within
+    this process's allowed set), or None when NVML cannot say."""
+    try:
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(device_index)
+        h = pynvml.nvmlDeviceGetHandleByUUID("GPU-" + str(props.uuid))
+        words = ((os.cpu_count() or 64) + 63) // 64
+        mask = pynvml.nvmlDeviceGetCpuAffinity(h, words)
+        cpus = {i * 64 + b for i, word in enumerate(mask) for b in range(64) if (word >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        return cpus or None
+    except Exception:
+        return None
+
+
+class near_gpu:
+    """Run a block with this process pinned to the GPU's local CPUs, so that
+    pinned host buffers allocated inside it sit on the GPU's NUMA node (the
+    host link then runs at full speed); the previous affinity is restored."""
+
+    def __init__(self, device_index):
+        self.cpus = gpu_local_cpus(device_index)
+        self.old = None
+
+    def __enter__(self):
+        if self.cpus:
+            self.old = os.sched_getaffinity(0)
+            os.sched_setaffinity(0, self.cpus)
+        return self
+
+    def __exit__(self, *exc):
+        if self.old is not None:
+            os.sched_setaffinity(0, self.old)
+        return False
+
+    def describe(self):
+        return (f"{len(self.cpus)} CPUs local to the GPU (NVML affinity)" if self.cpus
+                else "process default")
+
+
 def cpu_baseline(m, k, n, budget_s=10.0):
     """The oracle on this host's cores: a bounded number of full GEMMs."""
     import numpy as np
@@ -472,9 +516,11 @@ def main():
                 # the sharded GEMM with the fused gather, and reads the full
                 # Y back to the host.
                 x0, w0, _, _, _, a0 = sets[0]
-                hx = x0.view(torch.uint8).cpu().pin_memory()
-                hw = w0.view(torch.uint8).cpu().pin_memory()
-                hy = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
+                host = near_gpu(local_rank)
+                with host:  # pinned buffers on the GPU's NUMA side
+                    hx = x0.view(torch.uint8).cpu().pin_memory()
+                    hw = w0.view(torch.uint8).cpu().pin_memory()
+                    hy = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
                 dx = torch.empty_like(x0.view(torch.uint8))
                 dw = torch.empty_like(w0.view(torch.uint8))
                 g.w_local = dw.view(torch.float8_e4m3fn)
@@ -503,7 +549,8 @@ def main():
                             "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
                             "h2d_bytes_per_step": int(hx.numel() + hw.numel()),
                             "d2h_bytes_per_step": int(hy.numel() * 2),
-                            "api": "tinym_b200.sharded.ShardedFp8Gemm.fused (per rank; max over ranks)"}
+                            "api": "tinym_b200.sharded.ShardedFp8Gemm.fused (per rank; max over ranks)",
+                            "host_buffers": host.describe()}
             g.close_fused_gather()
         except Exception as e:  # reported, not fatal to the main measurement
             gather_cmp["error"] = f"{type(e).__name__}: {e}"
@@ -635,35 +682,37 @@ def main():
 
     # ---- end to end through the public API with host buffers (1 GPU)
     if world == 1 and args.e2e_steps > 0:
-        x, w, y, sx, sw, alpha = sets[0]
-        hx = x.view(torch.uint8).cpu().pin_memory()
-        hw = w.view(torch.uint8).cpu().pin_memory()
-        hy = torch.empty((m, n_local), dtype=torch.bfloat16).pin_memory()
-        dx = torch.empty_like(x.view(torch.uint8))
-        dw = torch.empty_like(w.view(torch.uint8))
+        with near_gpu(local_rank) as host:
+            x, w, y, sx, sw, alpha = sets[0]
+            hx = x.view(torch.uint8).cpu().pin_memory()
+            hw = w.view(torch.uint8).cpu().pin_memory()
+            hy = torch.empty((m, n_local), dtype=torch.bfloat16).pin_memory()
+            dx = torch.empty_like(x.view(torch.uint8))
+            dw = torch.empty_like(w.view(torch.uint8))
 
-        def e2e_step():
-            dx.copy_(hx, non_blocking=True)
-            dw.copy_(hw, non_blocking=True)
-            yy = candidate_kernel.fp8_gemm(dx.view(torch.float8_e4m3fn),
-                                           dw.view(torch.float8_e4m3fn), alpha)
-            hy.copy_(yy, non_blocking=True)
+            def e2e_step():
+                dx.copy_(hx, non_blocking=True)
+                dw.copy_(hw, non_blocking=True)
+                yy = candidate_kernel.fp8_gemm(dx.view(torch.float8_e4m3fn),
+                                               dw.view(torch.float8_e4m3fn), alpha)
+                hy.copy_(yy, non_blocking=True)
 
-        for _ in range(3):
-            e2e_step()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.e2e_steps):
-            e2e_step()
-        e1.record()
-        torch.cuda.synchronize()
-        e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
-        out["e2e"] = {"value": round(algo_bytes(m, k, n) / (e2e_ms * 1e-3) / 1e9, 3),
-                      "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
-                      "h2d_bytes_per_step": int(hx.numel() + hw.numel()),
-                      "d2h_bytes_per_step": int(hy.numel() * 2),
-                      "api": "candidate_kernel.fp8_gemm"}
+            for _ in range(3):
+                e2e_step()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.e2e_steps):
+                e2e_step()
+            e1.record()
+            torch.cuda.synchronize()
+            e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+            out["e2e"] = {"value": round(algo_bytes(m, k, n) / (e2e_ms * 1e-3) / 1e9, 3),
+                          "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
+                          "h2d_bytes_per_step": int(hx.numel() + hw.numel()),
+                          "d2h_bytes_per_step": int(hy.numel() * 2),
+                          "api": "candidate_kernel.fp8_gemm",
+                          "host_buffers": host.describe()}
         out["gpu_launches"] = args.steps  # timed region only (one launch per step)
         if not args.no_cpu_baseline:
             out["cpu_baseline"] = cpu_baseline(m, k, n, budget_s=args.cpu_budget)

@@ -351,6 +351,9 @@ def main():
     ap.add_argument("--no-act", action="store_true", help="skip the fused activation path")
     ap.add_argument("--no-fused-gather", action="store_true",
                     help="N > 1: skip the fused all-gather comparison")
+    ap.add_argument("--plan", default=None,
+                    help="explicit TC plan 'split,stages,block_k,tile_m' instead of the "
+                         "dispatch table (re-measures one point of a plan sweep)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     m, k, n = WORKLOADS[args.workload]
@@ -390,11 +393,17 @@ def main():
     stream = torch.cuda.current_stream(device)
     sm_count = torch.cuda.get_device_properties(device).multi_processor_count
     plan = tinym_b200.select_plan(m, n_local, k, sm_count)
+    explicit = None
+    if args.plan:
+        sp, st, bk, tm = (int(v) for v in args.plan.split(","))
+        explicit = tinym_b200.check_plan(m, n_local, k, tinym_b200.make_plan(
+            tinym_b200.KERNEL_TC, sp, st, 8 if m <= 8 else 16, block_k=bk, tile_m=tm))
+        plan = explicit
 
     def ours(s, stream_handle):
         x, w, y, sx, sw, alpha = s
         tinym_b200.gemm_ptr(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n_local, k,
-                            alpha_ptr=alpha.data_ptr(), stream=stream_handle)
+                            alpha_ptr=alpha.data_ptr(), plan=explicit, stream=stream_handle)
 
     # ---- cold-L2 per-launch latency (spacer protocol), untimed for `value`
     for i in range(args.warmup):

@@ -568,11 +568,20 @@ int tinym_select_plan(int64_t m, int64_t n, int64_t k, int32_t sm_count, tinym_p
     return fill_derived(m, n, k, out);
 }
 
-static int gemm_impl(const void* x, const void* w, void* y, int64_t ldy, int64_t m, int64_t n,
-                     int64_t k, const float* alpha_dev, float alpha, const tinym_plan* plan,
-                     void* stream, uint32_t flags, uint64_t timeout_ns, bool w_packed = false,
-                     const tinym_gather_desc* gd = nullptr) {
-    t_last_error[0] = '\0';
+// Everything one GEMM launch needs, built and validated by gemm_prepare
+// before anything is queued on the stream (the fused activation path
+// validates the GEMM before it launches its prologue).
+struct GemmLaunch {
+    CUtensorMap tm_w, tm_x;  // 64-byte aligned by their type
+    TinymParams prm;
+    tinym_plan plan;
+    const void* fn;
+};
+
+static int gemm_prepare(const void* x, const void* w, void* y, int64_t ldy, int64_t m, int64_t n,
+                        int64_t k, const float* alpha_dev, float alpha, const tinym_plan* plan,
+                        uint32_t flags, uint64_t timeout_ns, bool w_packed,
+                        const tinym_gather_desc* gd, GemmLaunch* out) {
     if (!x || !w || !y) return fail(TINYM_ERR_INVALID_ARGUMENT, "X, W and Y must be non-null");
     int st = check_shape(m, n, k);
     if (st != TINYM_OK) return st;
@@ -621,17 +630,17 @@ static int gemm_impl(const void* x, const void* w, void* y, int64_t ldy, int64_t
         return fail(TINYM_ERR_BAD_PLAN, "packed weights need the TC kernel");
     if (gd && p.kernel != TINYM_KERNEL_TC)
         return fail(TINYM_ERR_BAD_PLAN, "the fused all-gather needs the TC kernel");
-    CUtensorMap tm_w, tm_x;
     const int chunks = plan_chunks(p);
-    if ((st = get_map(w, n, k, p.tile_m, 1, chunks, dev, &tm_w, w_packed ? 1 : 0)) != TINYM_OK)
+    if ((st = get_map(w, n, k, p.tile_m, 1, chunks, dev, &out->tm_w, w_packed ? 1 : 0)) != TINYM_OK)
         return st;
     if (p.kernel == TINYM_KERNEL_TC) {
-        if ((st = get_map(x, m, k, p.mma_n, 1, chunks, dev, &tm_x)) != TINYM_OK) return st;
+        if ((st = get_map(x, m, k, p.mma_n, 1, chunks, dev, &out->tm_x)) != TINYM_OK) return st;
     } else {
-        if ((st = get_map(x, m, k, 1, 0, 1, dev, &tm_x)) != TINYM_OK) return st;
+        if ((st = get_map(x, m, k, 1, 0, 1, dev, &out->tm_x)) != TINYM_OK) return st;
     }
 
-    TinymParams prm{};
+    TinymParams& prm = out->prm;
+    prm = TinymParams{};
     prm.y = static_cast<__nv_bfloat16*>(y);
     prm.alpha_ptr = alpha_dev;
     prm.alpha = alpha;
@@ -664,15 +673,32 @@ static int gemm_impl(const void* x, const void* w, void* y, int64_t ldy, int64_t
         }
     }
 
-    const void* fn = nullptr;
-    if ((st = kernel_for(p, di, &fn)) != TINYM_OK) return st;
+    out->fn = nullptr;
+    if ((st = kernel_for(p, di, &out->fn)) != TINYM_OK) return st;
+    out->plan = p;
+    return TINYM_OK;
+}
+
+static int gemm_launch(GemmLaunch& g, void* stream) {
     cudaLaunchConfig_t cfg{};
     cudaLaunchAttribute attrs[2];
-    launch_config(p, stream, &cfg, attrs);
-    void* args[3] = {&tm_w, &tm_x, &prm};
-    e = cudaLaunchKernelExC(&cfg, fn, args);
+    launch_config(g.plan, stream, &cfg, attrs);
+    void* args[3] = {&g.tm_w, &g.tm_x, &g.prm};
+    const cudaError_t e = cudaLaunchKernelExC(&cfg, g.fn, args);
     if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
     return TINYM_OK;
+}
+
+static int gemm_impl(const void* x, const void* w, void* y, int64_t ldy, int64_t m, int64_t n,
+                     int64_t k, const float* alpha_dev, float alpha, const tinym_plan* plan,
+                     void* stream, uint32_t flags, uint64_t timeout_ns, bool w_packed = false,
+                     const tinym_gather_desc* gd = nullptr) {
+    t_last_error[0] = '\0';
+    GemmLaunch g;
+    const int st = gemm_prepare(x, w, y, ldy, m, n, k, alpha_dev, alpha, plan, flags, timeout_ns,
+                                w_packed, gd, &g);
+    if (st != TINYM_OK) return st;
+    return gemm_launch(g, stream);
 }
 
 int tinym_fp8_gemm_ex(const void* x, const void* w, void* y, int64_t ldy, int64_t m, int64_t n,
@@ -731,15 +757,18 @@ int tinym_fp8_gemm_quant_act(const void* x_act, int32_t act_dtype, const void* w
         return fail(TINYM_ERR_MISALIGNED, "X must be 16-byte and the workspace 256-byte aligned");
     if ((reinterpret_cast<uintptr_t>(w_scale_dev) & 3u))
         return fail(TINYM_ERR_MISALIGNED, "w_scale must be 4-byte aligned");
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-    DeviceInfo* di = nullptr;
-    if ((st = device_info(dev, &di)) != TINYM_OK) return st;
+    // The GEMM (shapes, alignment, plan, tensor maps) is validated before the
+    // prologue is queued, so a failing call leaves the workspace untouched.
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    GemmLaunch g;
+    if ((st = gemm_prepare(ws + tinym::kQuantWsHeader, w, y, ldy, m, n, k,
+                           reinterpret_cast<const float*>(ws) + 1, 0.0f, plan,
+                           tinym::kFlagEarlyW | kFlagQuantPrologue, kDefaultTimeoutNs, false,
+                           nullptr, &g)) != TINYM_OK)
+        return st;
     // Ordinary stream order (no programmatic attribute): everything before
     // this kernel has completed when it starts, which is what lets the GEMM
     // read W ahead of its griddepcontrol.wait.
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
     auto s = static_cast<cudaStream_t>(stream);
     if (act_dtype == TINYM_ACT_BF16)
         tinym::tinym_quant_act_kernel<__nv_bfloat16>
@@ -748,11 +777,9 @@ int tinym_fp8_gemm_quant_act(const void* x_act, int32_t act_dtype, const void* w
     else
         tinym::tinym_quant_act_kernel<float><<<tinym::kQuantCtas, tinym::kQuantThreads, 0, s>>>(
             static_cast<const float*>(x_act), m * k, ws, w_scale_dev);
-    e = cudaGetLastError();
+    const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "quantise kernel launch");
-    return gemm_impl(ws + tinym::kQuantWsHeader, w, y, ldy, m, n, k,
-                     reinterpret_cast<const float*>(ws) + 1, 0.0f, plan, stream,
-                     tinym::kFlagEarlyW | kFlagQuantPrologue, kDefaultTimeoutNs);
+    return gemm_launch(g, stream);
 }
 
 int tinym_fp8_gemm_quant_act_noalloc(const void* x_act, int32_t act_dtype, const void* w,

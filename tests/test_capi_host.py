@@ -281,6 +281,12 @@ def test_quant_act_host_checks():
                                         None) == 3
     assert lib.tinym_fp8_gemm_quant_act(256, 1, 256, 256, 256, 128, 1, 128, 128, 528, None,
                                         None) == 3
+    # the GEMM's own checks (misaligned W, ldy < N) also run before the
+    # quantise prologue is queued
+    assert lib.tinym_fp8_gemm_quant_act(256, 1, 264, 256, 256, 128, 1, 128, 128, 512, None,
+                                        None) == 3
+    assert lib.tinym_fp8_gemm_quant_act(256, 1, 256, 256, 256, 64, 1, 128, 128, 512, None,
+                                        None) == 1
 
 
 def test_ipc_export_rejects_null_arguments():

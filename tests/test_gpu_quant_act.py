@@ -126,6 +126,31 @@ def test_quant_act_torch_op_and_adapter(cuda_device, oracle):
         ck.fp8_gemm_act(x[:, :6128].contiguous(), w, w_scale)  # K mismatch
 
 
+def test_quant_act_rejected_plan_leaves_workspace_untouched(cuda_device):
+    """The GEMM is validated before the quantise prologue is queued: a call
+    whose plan is rejected writes neither the workspace nor Y."""
+    import torch
+
+    import tinym_b200
+
+    m, k, n = 9, 1024, 512
+    x = torch.randn((m, k), device=cuda_device).to(torch.bfloat16)
+    w = torch.zeros((n, k), dtype=torch.uint8, device=cuda_device).view(torch.float8_e4m3fn)
+    w_scale = torch.ones(1, dtype=torch.float32, device=cuda_device)
+    ws = torch.full((tinym_b200.quant_workspace_bytes(m, k),), 0xA5, dtype=torch.uint8,
+                    device=cuda_device)
+    y = torch.full((m, n), 7.0, dtype=torch.bfloat16, device=cuda_device)
+    bad = [tinym_b200.make_plan(tinym_b200.KERNEL_TC, 1, 4, 8),      # MMA N 8 < M 9
+           tinym_b200.make_plan(tinym_b200.KERNEL_TC, 9, 4, 16)]     # cluster of 9
+    for plan in bad:
+        with pytest.raises(tinym_b200.TinymError):
+            tinym_b200.gemm_quant_act(x, w, w_scale, out=y, workspace=ws, plan=plan)
+    torch.cuda.synchronize()
+    assert bool((ws == 0xA5).all())
+    assert bool((y == 7.0).all())
+    assert tinym_b200.device_status() == 0
+
+
 def test_quant_act_back_to_back_in_a_graph(cuda_device, oracle):
     """Repeated fused calls captured in a CUDA graph keep giving the same bits
     (the quantise kernel and the early-W GEMM chain through programmatic

@@ -194,6 +194,11 @@ def test_candidate_kernel_surface():
     with pytest.raises(ValueError):
         candidate_kernel.prepare_weights(torch.zeros(4, 4))
     assert candidate_kernel.build() is True
+    # alpha that is not a one-element CUDA float32 tensor: ValueError before
+    # any launch, as the reference's _host_alpha
+    for bad in (1.0, None, torch.ones(1)):
+        with pytest.raises(ValueError, match="alpha"):
+            candidate_kernel.fp8_gemm(torch.zeros(1, 16), torch.zeros(16, 16), bad)
 
 
 @pytest.mark.parametrize("m", [1, 3, 9, 16])

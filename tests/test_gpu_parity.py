@@ -282,6 +282,19 @@ def test_error_paths(cuda_device, oracle):
         candidate_kernel.fp8_gemm(torch.zeros(1, 256, device=dev, dtype=torch.bfloat16), b, al)
     with pytest.raises(ValueError):
         candidate_kernel.fp8_gemm(b[:1], b, al.double())
+    # non-finite alpha: the reference op's "alpha must be finite"
+    # (src/torch_candidate_extension.cu:30), also after an in-place change of
+    # an alpha tensor that was already accepted
+    for v in (float("nan"), float("inf")):
+        with pytest.raises(RuntimeError, match="alpha must be finite"):
+            candidate_kernel.fp8_gemm(b[:1], b, torch.full((1,), v, device=dev))
+    ok = torch.ones(1, device=dev)
+    candidate_kernel.fp8_gemm(b[:1], b, ok)
+    ok.fill_(float("nan"))
+    with pytest.raises(RuntimeError, match="alpha must be finite"):
+        candidate_kernel.fp8_gemm(b[:1], b, ok)
+    with pytest.raises(RuntimeError, match="alpha must be finite"):
+        torch.ops.sm120_fp8_gemm.run(b[:1], b, float("nan"))
     with pytest.raises(RuntimeError, match="UNSUPPORTED_SHAPE"):
         candidate_kernel.fp8_gemm(torch.zeros(1, 40, device=dev).to(f8),
                                   torch.zeros(8, 40, device=dev).to(f8), al)

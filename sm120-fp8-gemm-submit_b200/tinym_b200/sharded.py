@@ -103,8 +103,14 @@ class ShardedFp8Gemm:
         device = device or torch.device("cuda", torch.cuda.current_device())
         world = dist.get_world_size(self.group)
         rank = dist.get_rank(self.group)
+        # Both checks see the same values on every rank, so all ranks refuse
+        # together, before the first collective.
         if world > 8:
             raise ValueError("the fused all-gather supports up to 8 ranks")
+        if self.n < world:
+            raise ValueError(f"the fused all-gather needs N >= world size (N={self.n}, world={world})")
+        if not 1 <= m_max <= 16:
+            raise ValueError(f"m_max must be in 1..16 (got {m_max})")
         self._ybuf = torch.empty((2, m_max, self.n), dtype=torch.bfloat16, device=device)
         self._counter = torch.zeros(1, dtype=torch.int64, device=device)
         torch.cuda.synchronize(device)
@@ -144,6 +150,9 @@ class ShardedFp8Gemm:
 
         from . import gemm_allgather_ptr
 
+        if getattr(self, "_desc", None) is None:
+            # the peers' buffers are not mapped: the epilogue must not run
+            raise RuntimeError("fused gather is not enabled (enable_fused_gather first)")
         m, k = int(x.shape[0]), int(x.shape[1])
         if m > self._m_max:
             raise ValueError(f"M={m} > m_max={self._m_max}")
@@ -170,6 +179,7 @@ class ShardedFp8Gemm:
 
         from . import ipc_close
 
+        self._desc = None  # later fused() calls raise instead of storing to unmapped peers
         torch.cuda.synchronize()
         dist.barrier(group=self.group)
         for base in getattr(self, "_opened", []):

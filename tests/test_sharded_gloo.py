@@ -89,3 +89,59 @@ def test_sharded_gather_gloo_world2(m, k, n):
         assert rel <= 4e-3
     spans = sorted((a, b) for _, _, _, a, b in res)
     assert spans[0][0] == 0 and spans[-1][1] == n and spans[0][1] == spans[1][0]
+
+
+def test_fused_requires_enable():
+    """fused() on a wrapper whose peer buffers are not mapped raises on the
+    host (the epilogue would otherwise store to unmapped peer memory)."""
+    import torch
+
+    from tinym_b200.sharded import ShardedFp8Gemm
+
+    g = ShardedFp8Gemm(torch.zeros(4, 16), 4, 0, 4)
+    with pytest.raises(RuntimeError, match="not enabled"):
+        g.fused(torch.zeros(1, 16), 1.0)
+
+
+def _worker_refuse(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        import sys
+        from pathlib import Path
+
+        root = Path(__file__).resolve().parents[1]
+        sys.path.insert(0, str(root / "sm120-fp8-gemm-submit_b200"))
+        from tinym_b200.sharded import ShardedFp8Gemm
+
+        g = ShardedFp8Gemm.from_full_weight(torch.zeros(1, 16))  # N = 1 < world
+        try:
+            g.enable_fused_gather(device=torch.device("cpu"))
+            outcome = "enabled"
+        except ValueError as e:
+            outcome = "refused" if "N >= world" in str(e) else repr(e)
+        dist.barrier()  # every rank is still in step after the refusal
+        q.put((rank, outcome))
+        dist.destroy_process_group()
+    except Exception as e:  # pragma: no cover - reported to the parent
+        q.put((rank, repr(e)))
+
+
+def test_fused_gather_refused_on_every_rank_when_n_below_world():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_refuse, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert res == [(0, "refused"), (1, "refused")]

@@ -121,7 +121,8 @@ _torch_op_loaded = False
 
 
 def capi() -> ctypes.CDLL:
-    """Load libtinym_b200.so (building it first if it is missing or stale)."""
+    """Load libtinym_b200.so (building it first if it is missing; a stale
+    library is rebuilt by build.build_all, which __graft_entry__.build runs)."""
     global _capi
     if _capi is not None:
         return _capi
@@ -291,6 +292,44 @@ def quant_workspace_bytes(m: int, k: int) -> int:
     return int(out.value)
 
 
+def _check_operands(x, w) -> tuple[int, int, int]:
+    """(M, K, N) of contiguous row-major x [M, K] and w [N, K]; the kernels
+    read them as dense matrices, so views with other strides are refused."""
+    if x.dim() != 2 or w.dim() != 2:
+        raise ValueError("x and w must be rank-2 tensors")
+    if not x.is_contiguous() or not w.is_contiguous():
+        raise ValueError("x and w must be contiguous row-major tensors")
+    if x.shape[1] != w.shape[1]:
+        raise ValueError(f"x and w must have the same K (got {x.shape[1]} and {w.shape[1]})")
+    return int(x.shape[0]), int(x.shape[1]), int(w.shape[0])
+
+
+def _check_out(out, m: int, n: int, x):
+    """A fresh [M, N] BF16 output, or the caller's after checking that the
+    kernel's writes (M rows of N, row stride out.stride(0)) stay inside it."""
+    import torch
+
+    if out is None:
+        return torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    if out.dtype != torch.bfloat16 or out.dim() != 2 or tuple(out.shape) != (m, n) or \
+            out.stride(1) != 1 or out.stride(0) < n:
+        raise ValueError(f"out must be a [{m}, {n}] bfloat16 tensor with unit column stride")
+    return out
+
+
+def _check_devices(*tensors) -> None:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("every tensor argument must be a CUDA tensor")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError("every tensor argument must be on the same CUDA device")
+
+
 def gemm_quant_act(x, w, w_scale, *, out=None, workspace=None, plan: Plan | None = None):
     """Fused activation path: quantise BF16 / FP32 x per tensor on the device,
     then Y = alpha * q(x) . W^T.  Returns (Y, workspace); the workspace holds
@@ -303,12 +342,20 @@ def gemm_quant_act(x, w, w_scale, *, out=None, workspace=None, plan: Plan | None
         dt = ACT_F32
     else:
         raise ValueError("x must be bfloat16 or float32")
-    m, k = x.shape
-    n = w.shape[0]
-    if out is None:
-        out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    if w.dtype != torch.float8_e4m3fn:
+        raise ValueError("w must be float8_e4m3fn")
+    m, k, n = _check_operands(x, w)
+    if not isinstance(w_scale, torch.Tensor) or w_scale.dtype != torch.float32 or \
+            w_scale.numel() != 1:
+        raise ValueError("w_scale must be a one-element float32 tensor")
+    need = quant_workspace_bytes(m, k)
+    if workspace is not None and (workspace.dtype != torch.uint8 or workspace.dim() != 1 or
+                                  not workspace.is_contiguous() or workspace.numel() < need):
+        raise ValueError(f"workspace must be a contiguous uint8 vector of >= {need} bytes")
+    out = _check_out(out, m, n, x)
+    _check_devices(x, w, w_scale, out, workspace)
     if workspace is None:
-        workspace = torch.empty(quant_workspace_bytes(m, k), dtype=torch.uint8, device=x.device)
+        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
     stream = torch.cuda.current_stream(x.device).cuda_stream
     pl = ctypes.byref(plan) if plan is not None else None
     _check(capi().tinym_fp8_gemm_quant_act(x.data_ptr(), dt, w.data_ptr(), w_scale.data_ptr(),
@@ -369,10 +416,11 @@ def gemm(x, w, alpha, *, out=None, plan: Plan | None = None, static_w: bool = Fa
 
     if x.dtype != torch.float8_e4m3fn or w.dtype != torch.float8_e4m3fn:
         raise ValueError("x and w must be float8_e4m3fn")
-    m, k = x.shape
-    n = w.shape[0]
-    if out is None:
-        out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    m, k, n = _check_operands(x, w)
+    if isinstance(alpha, torch.Tensor) and (alpha.dtype != torch.float32 or alpha.numel() < 1):
+        raise ValueError("a tensor alpha must be float32 with at least one element")
+    out = _check_out(out, m, n, x)
+    _check_devices(x, w, alpha if isinstance(alpha, torch.Tensor) else None, out)
     stream = torch.cuda.current_stream(x.device).cuda_stream
     if isinstance(alpha, torch.Tensor):
         gemm_ptr(x.data_ptr(), w.data_ptr(), out.data_ptr(), m, n, k, ldy=out.stride(0),

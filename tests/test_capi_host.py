@@ -323,3 +323,33 @@ def test_bench_reference_arm_prints_one_line():
     assert d["impl"] == "reference" and d["unit"] == "GB/s" and d["value"] > 0
     assert d["cpu_baseline"]["kind"] in ("port", "reference")
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["gpu_launches"] == 0
+
+
+def test_torch_wrappers_validate_before_launch():
+    """tinym_b200.gemm / gemm_quant_act refuse operands the kernel would read
+    or write out of bounds (K mismatch, strided views, a short out or
+    workspace) and host tensors, before any pointer reaches the C ABI."""
+    import torch
+
+    import tinym_b200 as t
+
+    f8 = torch.float8_e4m3fn
+    x = torch.zeros(2, 32).to(f8)
+    w = torch.zeros(8, 32).to(f8)
+    with pytest.raises(ValueError, match="same K"):
+        t.gemm(x, torch.zeros(8, 16).to(f8), 1.0)
+    with pytest.raises(ValueError, match="contiguous"):
+        t.gemm(x, torch.zeros(32, 8).to(f8).t(), 1.0)
+    with pytest.raises(ValueError, match=r"\[2, 8\]"):
+        t.gemm(x, w, 1.0, out=torch.empty(2, 4, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match=r"\[2, 8\]"):
+        t.gemm(x, w, 1.0, out=torch.empty(8, 2, dtype=torch.bfloat16).t())
+    with pytest.raises(ValueError, match="CUDA"):
+        t.gemm(x, w, 1.0)
+    xa = torch.zeros(2, 32, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="workspace"):
+        t.gemm_quant_act(xa, w, torch.ones(1), workspace=torch.empty(300, dtype=torch.uint8))
+    with pytest.raises(ValueError, match="w_scale"):
+        t.gemm_quant_act(xa, w, torch.ones(2))
+    with pytest.raises(ValueError, match="CUDA"):
+        t.gemm_quant_act(xa, w, torch.ones(1))

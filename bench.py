@@ -309,10 +309,34 @@ def cpu_baseline(m, k, n, budget_s=10.0):
         if len(times) >= 200:
             break
     med = statistics.median(times)
+    # The FP32 matmul alone on operands dequantised once, outside the timing:
+    # how much of the oracle's time is the E4M3 -> FP32 widening.
+    xf, wf = orc.e4m3_to_f32(xq), orc.e4m3_to_f32(wq)
+    mm = []
+    for _ in range(max(5, min(50, len(times)))):
+        t0 = time.perf_counter()
+        np.matmul(xf, wf.T)
+        mm.append(time.perf_counter() - t0)
     return {"value": algo_bytes(m, k, n) / med / 1e9, "unit": "GB/s", "cores": int(threads),
             "kind": "port", "median_ms": med * 1e3,
+            "matmul_only_median_ms": statistics.median(mm) * 1e3,
+            "cpu_model": cpu_model(),
             "sample": f"{len(times)} full ({m},{k},{n}) GEMMs: numpy LUT dequant + FP32 matmul "
                       f"+ alpha (oracle/fp8_oracle.reference), median"}
+
+
+def cpu_model() -> str:
+    """The host CPU's model name (first processor entry of /proc/cpuinfo)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
 
 
 def run_reference_arm(args, m, k, n):
@@ -329,7 +353,10 @@ def run_reference_arm(args, m, k, n):
         "data": "synthetic", "impl": "reference",
         "config": {"workload": args.workload, "M": m, "K": k, "N": n},
         "cpu_baseline": {"value": round(cb["value"], 3), "unit": "GB/s", "cores": cb["cores"],
-                         "kind": cb["kind"], "sample": cb["sample"]},
+                         "kind": cb["kind"], "sample": cb["sample"],
+                         "median_ms": round(cb["median_ms"], 3),
+                         "matmul_only_median_ms": round(cb["matmul_only_median_ms"], 3),
+                         "cpu_model": cb["cpu_model"]},
         "e2e": {"value": round(cb["value"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "gpu_launches": 0,

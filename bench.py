@@ -23,11 +23,18 @@ describe.
 * roofline         -- dominant kernel vs the measured HBM copy bandwidth.
 * cpu_baseline     -- the CPU oracle (oracle/fp8_oracle.reference: dequant +
                       FP32 matmul + alpha) on this host, rank 0 at N=1.
+* harness_protocol_us, act_quant_gemm, graph_us_per_launch_static_w (1 GPU)
+                   -- the reference harness's memset protocol for ours and
+                      cuBLASLt, the fused activation path, and the
+                      TINYM_FLAG_STATIC_W back-to-back rate.
 
 Multi-GPU (torchrun, one rank per GPU): W is N-sharded (column-parallel);
 each rank computes its [M, N/g] slab with no collective in the timed region
-("scaling": "strong", total work fixed).  The optional BF16 all-gather of Y
-over NCCL is timed separately and reported as allgather_us.
+("scaling": "strong", total work fixed).  Beside it: allgather_us (the NCCL
+all-gather of Y alone), gather_of_y (GEMM + NCCL all-gather against the GEMM
+with the gather fused into its epilogue) and e2e through
+ShardedFp8Gemm.fused with host buffers.  --impl reference runs the CPU
+oracle on rank 0 only.
 """
 
 from __future__ import annotations

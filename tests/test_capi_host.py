@@ -353,3 +353,31 @@ def test_torch_wrappers_validate_before_launch():
         t.gemm_quant_act(xa, w, torch.ones(2))
     with pytest.raises(ValueError, match="CUDA"):
         t.gemm_quant_act(xa, w, torch.ones(1))
+
+
+def test_plain_c_caller(tmp_path):
+    """A C99 program (tests/c_abi_host.c) compiles against include/tinym_b200.h,
+    links libtinym_b200.so and runs the host-side entry points: the boundary
+    needs neither Python nor torch."""
+    import shutil
+    import subprocess
+
+    import tinym_b200
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    lib = tinym_b200.capi()  # builds the library if it is missing
+    assert lib is not None
+    root = Path(__file__).resolve().parents[1]
+    libdir = tinym_b200.CORE_SO.parent
+    exe = tmp_path / "c_abi_host"
+    subprocess.run([cc, "-std=c99", "-Wall", "-Wextra", "-Werror", "-pedantic",
+                    "-I", str(root / "include"), str(root / "tests" / "c_abi_host.c"),
+                    "-o", str(exe), "-L", str(libdir), "-ltinym_b200",
+                    f"-Wl,-rpath,{libdir}"], check=True, capture_output=True, text=True)
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0, run.stderr
+    lines = run.stdout.strip().splitlines()
+    assert lines[-1] == "c abi host checks ok"
+    assert "M=9 K=6144 N=5120 split=3 stages=4 block_k=256 tile_m=128 ctas=120" in lines

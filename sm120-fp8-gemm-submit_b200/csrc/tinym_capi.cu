@@ -427,10 +427,7 @@ int kernel_for(const tinym_plan& p, DeviceInfo* di, const void** fn) {
         e = cudaFuncSetAttribute(*fn, cudaFuncAttributePreferredSharedMemoryCarveout,
                                  cudaSharedmemCarveoutMaxShared);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(PreferredSharedMemoryCarveout)");
-        if (p.split_k > kMaxSplit) {
-            e = cudaFuncSetAttribute(*fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-            if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(NonPortableClusterSize)");
-        }
+        // (clusters stay within the portable size: fill_derived caps split_k at 8)
         di->attr_done.fetch_or(attr_bit, std::memory_order_acq_rel);
     }
     return TINYM_OK;

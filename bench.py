@@ -28,11 +28,15 @@ describe.
                       cuBLASLt, the fused activation path, and the
                       TINYM_FLAG_STATIC_W back-to-back rate.
 
-Multi-GPU (torchrun, one rank per GPU): W is N-sharded (column-parallel);
-each rank computes its [M, N/g] slab with no collective in the timed region
-("scaling": "strong", total work fixed).  Beside it: allgather_us (the NCCL
-all-gather of Y alone), gather_of_y (GEMM + NCCL all-gather against the GEMM
-with the gather fused into its epilogue) and e2e through
+Multi-GPU (torchrun, one rank per GPU): W is N-sharded (column-parallel)
+and each rank computes its [M, slab] part of Y with no collective in the
+timed region.  Default "scaling": "weak": every rank owns a slab of the
+workload's full N, so the sharded GEMM has N_total = N * ranks and per-GPU
+work is fixed; --scaling strong splits the workload's N over the ranks
+instead.  Beside a weak value, strong_scaling gives that fixed problem's
+N-sharded latency and aggregate GB/s.  Also at N > 1: allgather_us (the
+NCCL all-gather of Y alone), gather_of_y (GEMM + NCCL all-gather against
+the GEMM with the gather fused into its epilogue) and e2e through
 ShardedFp8Gemm.fused with host buffers.  --impl reference runs the CPU
 oracle on rank 0 only.
 """
@@ -356,7 +360,7 @@ def run_reference_arm(args, m, k, n):
         "metric": f"achieved HBM GB/s, cold-L2 FP8 GEMM (M={m},K={k},N={n})",
         "value": round(cb["value"], 3), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(cb["median_ms"], 4),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "impl": "reference",
         "config": {"workload": args.workload, "M": m, "K": k, "N": n},
         "cpu_baseline": {"value": round(cb["value"], 3), "unit": "GB/s", "cores": cb["cores"],
@@ -388,6 +392,11 @@ def main():
     ap.add_argument("--plan", default=None,
                     help="explicit TC plan 'split,stages,block_k,tile_m' instead of the "
                          "dispatch table (re-measures one point of a plan sweep)")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
+                    help="N > 1: weak = every rank owns a full workload-N slab of a GEMM "
+                         "whose N grows with the rank count (value); strong = the "
+                         "workload's N split over the ranks (also reported beside a weak "
+                         "value as strong_scaling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     m, k, n = WORKLOADS[args.workload]
@@ -416,10 +425,15 @@ def main():
     import tinym_b200
 
     candidate_kernel.build()
-    # This rank's column slab of W (N-sharding); rows rounded to whole tiles.
-    n_local = n // world
-    if n_local * world != n:
-        raise SystemExit(f"N={n} is not divisible by {world} ranks")
+    # This rank's column slab of W (N-sharding).  Weak scaling: the slab is
+    # the workload's full N and the sharded GEMM has N_total = N * ranks.
+    # Strong scaling: the workload's N is split over the ranks.
+    if args.scaling == "weak":
+        n_local, n_total = n, n * world
+    else:
+        n_local, n_total = n // world, n
+        if n_local * world != n:
+            raise SystemExit(f"N={n} is not divisible by {world} ranks")
     l2 = torch.cuda.get_device_properties(device).L2_cache_size
     set_bytes = n_local * k + m * k
     n_sets = max(2, math.ceil(2.5 * l2 / set_bytes) + 1)
@@ -482,6 +496,34 @@ def main():
     value_gbs = total_bytes / (span_max * 1e-3) / 1e9
     mean_us = span_max / args.steps * 1e3  # average launch duration in the timed region
 
+    # Beside a weak-scaling value: the N-sharded latency of the fixed
+    # problem (the workload's N split over the ranks), back-to-back, max over
+    # ranks -- how far one GEMM of this size speeds up on more GPUs.
+    strong = None
+    if dist is not None and args.scaling == "weak" and n % world == 0:
+        n_s = n // world
+        ss_sets = make_operands(m, k, n_s, max(2, math.ceil(2.5 * l2 / (n_s * k + m * k)) + 1),
+                                device, seed=101 + rank)
+
+        def ours_strong(s, stream_handle):
+            x, w, y, sx, sw, alpha = s
+            tinym_b200.gemm_ptr(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n_s, k,
+                                alpha_ptr=alpha.data_ptr(), stream=stream_handle)
+
+        s_steps = min(args.steps, 20000)
+        torch.cuda.synchronize()
+        dist.barrier()
+        s_span = graph_throughput(ours_strong, ss_sets, s_steps, args.warmup)
+        s_t = torch.tensor([s_span / s_steps], device=device, dtype=torch.float64)
+        dist.all_reduce(s_t, op=dist.ReduceOp.MAX)
+        s_us = float(s_t.item()) * 1e3
+        strong = {"N": n, "n_per_gpu": n_s, "us_per_launch": round(s_us, 3),
+                  "aggregate_gbs": round(algo_bytes(m, k, n_s) * world / (s_us * 1e-6) / 1e9, 1),
+                  "plan": tinym_b200.select_plan(m, n_s, k, sm_count).as_dict(),
+                  "protocol": "CUDA-graph back-to-back launches, cold W (rotating buffers), "
+                              "max over ranks"}
+        del ss_sets
+
     # optional all-gather of Y (timed separately)
     allgather_us = None
     if dist is not None:
@@ -539,7 +581,7 @@ def main():
 
         gather_cmp["gemm_plus_nccl_allgather_us"] = round(device_time(nccl_step), 3)
         try:
-            g = ShardedFp8Gemm(sets[0][1], n, rank * n_local, (rank + 1) * n_local)
+            g = ShardedFp8Gemm(sets[0][1], n_total, rank * n_local, (rank + 1) * n_local)
             g.enable_fused_gather(m_max=m, device=device)
 
             def fused_step(i):
@@ -563,7 +605,7 @@ def main():
                 with host:  # pinned buffers on the GPU's NUMA side
                     hx = x0.view(torch.uint8).cpu().pin_memory()
                     hw = w0.view(torch.uint8).cpu().pin_memory()
-                    hy = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
+                    hy = torch.empty((m, n_total), dtype=torch.bfloat16).pin_memory()
                 dx = torch.empty_like(x0.view(torch.uint8))
                 dw = torch.empty_like(w0.view(torch.uint8))
                 g.w_local = dw.view(torch.float8_e4m3fn)
@@ -588,7 +630,7 @@ def main():
                                   dtype=torch.float64)
                 dist.all_reduce(tt, op=dist.ReduceOp.MAX)
                 e2e_ms = float(tt.item())
-                e2e_dist = {"value": round(algo_bytes(m, k, n) / (e2e_ms * 1e-3) / 1e9, 3),
+                e2e_dist = {"value": round(algo_bytes(m, k, n_total) / (e2e_ms * 1e-3) / 1e9, 3),
                             "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
                             "h2d_bytes_per_step": int(hx.numel() + hw.numel()),
                             "d2h_bytes_per_step": int(hy.numel() * 2),
@@ -610,10 +652,11 @@ def main():
             "value": round(value_gbs, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(span_max / args.steps, 6),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
             "dtype": "e4m3 in / f32 acc / bf16 out", "data": "synthetic",
-            "config": {"workload": args.workload, "M": m, "K": k, "N": n, "n_per_gpu": n_local,
-                       "parallelism": f"N-sharded x{world}" if world > 1 else "single GPU",
+            "config": {"workload": args.workload, "M": m, "K": k, "N": n_total, "n_per_gpu": n_local,
+                       "parallelism": (f"N-sharded x{world} ({args.scaling} scaling)" if world > 1
+                                       else "single GPU"),
                        "cold_l2": f"rotation over {n_sets} buffer sets "
                                   f"({n_sets * set_bytes / 2**20:.0f} MiB > 2x L2 "
                                   f"{l2 / 2**20:.0f} MiB)",
@@ -628,9 +671,10 @@ def main():
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_source": f"{peak_note} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
-                         # ncu captures are of the 1-GPU launch; a rank of an
-                         # N-sharded run moves only its slab, so none applies
-                         "traffic": committed_traffic(args.workload) if world == 1 else None,
+                         # ncu captures are of the workload's 1-GPU launch: it
+                         # applies to every rank of a weak-scaling run (same
+                         # slab), to no rank of a strong-scaling one
+                         "traffic": committed_traffic(args.workload) if n_local == n else None,
                          "algorithmic_bytes_per_launch": algo_bytes(m, k, n_local)},
             "gpu_launches": args.steps,
             "clocks": clk.summary(),
@@ -641,6 +685,8 @@ def main():
             out["gather_of_y"] = gather_cmp
         if e2e_dist is not None:
             out["e2e"] = e2e_dist
+        if strong is not None:
+            out["strong_scaling"] = strong
 
     # ---- cuBLASLt competitor (1 GPU only, same buffers / protocol)
     if rank == 0 and world == 1 and not args.no_cublas:

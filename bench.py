@@ -84,6 +84,22 @@ def algo_bytes(m: int, k: int, n: int) -> int:
     return m * k + n * k + 2 * m * n
 
 
+def rank_slab(n: int, world: int, scaling: str) -> tuple[int, int]:
+    """(W rows per rank, N of the sharded GEMM) for a workload of N rows on
+    `world` ranks.  weak: every rank owns a slab of the workload's full N,
+    so the GEMM has N * world rows and per-GPU work is fixed.  strong: the
+    workload's N is split evenly over the ranks."""
+    if world < 1:
+        raise ValueError("world size must be positive")
+    if scaling == "weak":
+        return n, n * world
+    if scaling != "strong":
+        raise ValueError(f"unknown scaling {scaling!r}")
+    if n % world:
+        raise ValueError(f"N={n} is not divisible by {world} ranks")
+    return n // world, n
+
+
 def measured_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -425,15 +441,10 @@ def main():
     import tinym_b200
 
     candidate_kernel.build()
-    # This rank's column slab of W (N-sharding).  Weak scaling: the slab is
-    # the workload's full N and the sharded GEMM has N_total = N * ranks.
-    # Strong scaling: the workload's N is split over the ranks.
-    if args.scaling == "weak":
-        n_local, n_total = n, n * world
-    else:
-        n_local, n_total = n // world, n
-        if n_local * world != n:
-            raise SystemExit(f"N={n} is not divisible by {world} ranks")
+    try:
+        n_local, n_total = rank_slab(n, world, args.scaling)
+    except ValueError as e:
+        raise SystemExit(str(e)) from None
     l2 = torch.cuda.get_device_properties(device).L2_cache_size
     set_bytes = n_local * k + m * k
     n_sets = max(2, math.ceil(2.5 * l2 / set_bytes) + 1)

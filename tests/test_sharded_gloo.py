@@ -145,3 +145,29 @@ def test_fused_gather_refused_on_every_rank_when_n_below_world():
         p.join(timeout=60)
         assert p.exitcode == 0
     assert res == [(0, "refused"), (1, "refused")]
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_bench_rank_slabs(world):
+    """The multi-GPU bench's slab arithmetic: weak scaling keeps every rank's
+    slab at the workload's N (the sharded GEMM grows), strong scaling splits
+    the workload's N; the shard bounds of the sharded wrapper tile the
+    GEMM's N exactly with those slabs at the official N."""
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    import bench
+    from tinym_b200.sharded import shard_bounds
+
+    for n in (5120, 8192, 16384):
+        n_local, n_total = bench.rank_slab(n, world, "weak")
+        assert (n_local, n_total) == (n, n * world)
+        assert [shard_bounds(n_total, world, r) for r in range(world)] == \
+            [(r * n, (r + 1) * n) for r in range(world)]
+        n_local, n_total = bench.rank_slab(n, world, "strong")
+        assert n_local * world == n_total == n
+    with pytest.raises(ValueError):
+        bench.rank_slab(5120, 3, "strong")
+    with pytest.raises(ValueError):
+        bench.rank_slab(5120, world, "diagonal")

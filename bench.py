@@ -1,7 +1,8 @@
 """Benchmark of the B200 tiny-M FP8 GEMM (driver contract: one JSON line).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload m9_k6144_n5120]
+                    [--workload m9_k5120_n16384] [--scaling strong|weak]
+    python bench.py --sweep      # M = 1..16 x three (K, N) pairs, one JSON line each
 
 A "step" is one GEMM Y[M,N] = alpha * X[M,K] . W[N,K]^T over one of R
 rotating (X, W, Y) buffer sets whose total size exceeds 2x the L2 cache, so
@@ -9,14 +10,23 @@ every step reads W cold from HBM (the reference harness's cold-L2 protocol,
 fp8_gemm_task_harness.py:76-96, done by rotation instead of a 256 MiB
 memset).  Inputs are synthetic: X, W ~ N(0,1) FP32, quantised per tensor
 (scale = amax/448, round-to-nearest-even E4M3), as BASELINE.json's configs
-describe.
+describe.  The default workload is (9, 5120, 16384), BASELINE configs[3]:
+the point of the north-star roofline target and the problem that is
+N-sharded over 2/4/8 GPUs.
 
 * value            -- whole-job HBM throughput: algorithmic bytes
-                      (M*K + N*K + 2*M*N, fp8_gemm_task_harness.py:153) of
-                      every step on every rank / max-over-ranks device time.
-* median_us        -- cold-L2 median per-launch latency (CUDA events).
-* cublas_median_us -- torch._scaled_mm (cuBLASLt) on the same buffers and
-                      protocol (the harness's competitor, :68-69), 1 GPU.
+                      (M*K + N*K + 2*M*N, fp8_gemm_task_harness.py:153) per
+                      step on every rank / the step time.  The K timed steps
+                      run back to back as a few CUDA-graph replays; the step
+                      time (ms_per_step) is the median over the replays of
+                      ms per launch, max over ranks (timing.p10/p90/mean).
+* median_us        -- cold-L2 median latency of single launches (CUDA events,
+                      each launch after a GPU spin spacer): the metric's own
+                      statistic.
+* cublas_*         -- torch._scaled_mm (cuBLASLt) on the same buffers and
+                      protocols (the harness's competitor, :68-69), 1 GPU.
+* points           -- the six official (M, K, N) points, ours and cuBLASLt:
+                      median_us, graph_us, frac of the measured HBM peak.
 * e2e              -- the same metric through the public API
                       (candidate_kernel.fp8_gemm) with pinned host inputs:
                       H2D of X and W, the GEMM, D2H of Y, every step.
@@ -30,15 +40,15 @@ describe.
 
 Multi-GPU (torchrun, one rank per GPU): W is N-sharded (column-parallel)
 and each rank computes its [M, slab] part of Y with no collective in the
-timed region.  Default "scaling": "weak": every rank owns a slab of the
-workload's full N, so the sharded GEMM has N_total = N * ranks and per-GPU
-work is fixed; --scaling strong splits the workload's N over the ranks
-instead.  Beside a weak value, strong_scaling gives that fixed problem's
-N-sharded latency and aggregate GB/s.  Also at N > 1: allgather_us (the
-NCCL all-gather of Y alone), gather_of_y (GEMM + NCCL all-gather against
-the GEMM with the gather fused into its epilogue) and e2e through
-ShardedFp8Gemm.fused with host buffers.  --impl reference runs the CPU
-oracle on rank 0 only.
+timed region.  Default "scaling": "strong": the workload's N is split over
+the ranks, so the value at N GPUs is the fixed problem's N-sharded
+aggregate rate; weak_scaling beside it gives every rank a full workload-N
+slab (--scaling weak swaps the two).  Also at N > 1: allgather_us (the NCCL
+all-gather of Y alone), gather_of_y (GEMM + NCCL all-gather against the
+GEMM with the gather fused into its epilogue), gather_check (one fused call
+of the public sharded API compared with the FP32 reference of the whole
+problem) and e2e through ShardedFp8Gemm.fused with host buffers.
+--impl reference runs the CPU oracle on rank 0 only.
 """
 
 from __future__ import annotations
@@ -76,7 +86,7 @@ WORKLOADS = {
     "m9_k5120_n16384": (9, 5120, 16384),
     "m16_k5120_n16384": (16, 5120, 16384),
 }
-DEFAULT_WORKLOAD = "m9_k6144_n5120"
+DEFAULT_WORKLOAD = "m9_k5120_n16384"  # the north-star point, also sharded over 2/4/8 GPUs
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -179,8 +189,9 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def make_operands(m, k, n, n_sets, device, seed=0):
-    """N(0,1) FP32 -> per-tensor amax/448 -> E4M3 (torch ops on the device)."""
+def make_operands(m, k, n, n_sets, device, seed=0, w_dist="normal"):
+    """FP32 draws -> per-tensor amax/448 -> E4M3 (torch ops on the device).
+    X ~ N(0,1); W ~ N(0,1), Uniform(-1,1) or Student-t(3) (w_dist)."""
     import torch
 
     g = torch.Generator(device=device).manual_seed(seed)
@@ -189,10 +200,24 @@ def make_operands(m, k, n, n_sets, device, seed=0):
         s = (t.abs().amax() / 448.0).clamp(min=1e-12)
         return (t / s).clamp(-448.0, 448.0).to(torch.float8_e4m3fn), s.reshape(1).float()
 
+    def draw_w():
+        if w_dist == "normal":
+            return torch.randn(n, k, device=device, generator=g)
+        if w_dist == "uniform":
+            return torch.rand(n, k, device=device, generator=g) * 2.0 - 1.0
+        if w_dist == "student_t":
+            # t(3) = Z / sqrt(chi2(3) / 3), chi2(3) a sum of three squared normals
+            z = torch.randn(n, k, device=device, generator=g)
+            chi = torch.zeros(n, k, device=device)
+            for _ in range(3):
+                chi += torch.randn(n, k, device=device, generator=g).square()
+            return z / (chi / 3.0).sqrt()
+        raise ValueError(f"unknown w_dist {w_dist!r}")
+
     sets = []
     for i in range(n_sets):
         x32 = torch.randn(m, k, device=device, generator=g)
-        w32 = torch.randn(n, k, device=device, generator=g)
+        w32 = draw_w()
         x, sx = quant(x32)
         w, sw = quant(w32)
         del x32, w32
@@ -234,40 +259,63 @@ def per_launch_latency(fn, sets, n, flush=None):
     return [s.elapsed_time(e) for s, e in zip(starts, ends)]
 
 
-def graph_throughput(fn, sets, steps, warmup):
-    """Time exactly `steps` back-to-back launches (rotating over `sets`)
-    replayed from CUDA graphs; returns total device ms.  Graph replay keeps
-    the GPU fed, so this is the kernel's sustained rate, not the host's."""
+def graph_chunks(fn, sets, steps, warmup, target_chunks=5):
+    """Time exactly `steps` back-to-back launches as a few CUDA-graph replays.
+
+    The steps are cut into chunks of R = max(1, steps // target_chunks)
+    launches (the last one may be shorter), each chunk a graph over the
+    rotating `sets`.  All replays are queued behind a spin spacer, so they
+    run back to back on the device, with an event between consecutive
+    replays.  Returns (total_ms, [(launches, ms) per chunk]); the median of
+    the per-chunk ms per launch is robust against a single slow replay.
+    """
     import torch
 
-    chunk = min(steps, 4 * len(sets))
-    graphs = []
-    for size in sorted({chunk, steps % chunk} - {0}, reverse=True):
-        g = torch.cuda.CUDAGraph()
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
-            for i in range(3):  # warm-up on the capture stream
-                fn(sets[i % len(sets)], s.cuda_stream)
-        torch.cuda.current_stream().wait_stream(s)
-        with torch.cuda.graph(g):
-            cs = torch.cuda.current_stream().cuda_stream
-            for i in range(size):
-                fn(sets[i % len(sets)], cs)
-        graphs.append((size, g))
-    full = {size: g for size, g in graphs}
-    for _ in range(max(1, warmup // chunk)):
-        full[chunk].replay()
+    r = max(1, steps // max(1, target_chunks))
+    sizes = [r] * (steps // r) + ([steps % r] if steps % r else [])
+    graphs = {}
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for i in range(3):  # warm-up on the capture stream
+            fn(sets[i % len(sets)], stream.cuda_stream)
+    torch.cuda.current_stream().wait_stream(stream)
+    plan = []
+    i0 = 0
+    for size in sizes:
+        key = (i0 % len(sets), size)
+        if key not in graphs:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                cs = torch.cuda.current_stream().cuda_stream
+                for j in range(size):
+                    fn(sets[(i0 + j) % len(sets)], cs)
+            graphs[key] = g
+        plan.append((size, graphs[key]))
+        i0 += size
+    for _ in range(max(1, warmup // max(1, r))):
+        for g in graphs.values():
+            g.replay()
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps // chunk):
-        full[chunk].replay()
-    if steps % chunk:
-        full[steps % chunk].replay()
-    e1.record()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(plan) + 1)]
+    # the spacer keeps the GPU busy while the host queues every replay
+    torch.cuda._sleep(SPACER_CYCLES * (1 + len(plan)))
+    evs[0].record()
+    for c, (size, g) in enumerate(plan):
+        g.replay()
+        evs[c + 1].record()
     torch.cuda.synchronize()
-    return e0.elapsed_time(e1)
+    chunks = [(size, evs[c].elapsed_time(evs[c + 1])) for c, (size, _) in enumerate(plan)]
+    total = evs[0].elapsed_time(evs[-1])
+    del graphs
+    return total, chunks
+
+
+def chunk_stats(chunks):
+    """(median, p10, p90) of ms per launch over the full-size chunks."""
+    full = max(size for size, _ in chunks)
+    per = sorted(ms / size for size, ms in chunks if size == full)
+    return (statistics.median(per), per[len(per) // 10], per[min(len(per) - 1, (9 * len(per)) // 10)])
 
 
 def gpu_local_cpus(device_index):
@@ -391,10 +439,81 @@ def run_reference_arm(args, m, k, n):
     print(json.dumps(line), flush=True)
 
 
+OFFICIAL_POINTS = [(1, 6144, 5120), (9, 6144, 5120), (1, 5120, 8192), (9, 5120, 8192),
+                   (1, 5120, 16384), (9, 5120, 16384)]
+
+
+def measure_point(m, k, n, device, l2, peak, *, cublas=True, w_dist="normal", lat_n=60,
+                  graph_steps=100, seed=0):
+    """Ours and cuBLASLt at one (M, K, N) on the same rotating cold-W buffers:
+    the spacer-protocol median of single launches and the median
+    back-to-back launch time (graph_chunks), plus the roofline fraction of
+    the back-to-back time."""
+    import torch
+
+    import tinym_b200
+
+    set_bytes = n * k + m * k
+    n_sets = max(2, math.ceil(2.5 * l2 / set_bytes) + 1)
+    sets = make_operands(m, k, n, n_sets, device, seed=seed, w_dist=w_dist)
+
+    def ours(s, h):
+        x, w, y, sx, sw, alpha = s
+        tinym_b200.gemm_ptr(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k,
+                            alpha_ptr=alpha.data_ptr(), stream=h)
+
+    def cublas_fn(s, h):
+        x, w, y, sx, sw, alpha = s
+        torch._scaled_mm(x, w.t(), scale_a=sx, scale_b=sw, out_dtype=torch.bfloat16)
+
+    stream = torch.cuda.current_stream(device).cuda_stream
+    out = {"M": m, "K": k, "N": n, "w_dist": w_dist,
+           "plan": tinym_b200.select_plan(m, n, k, torch.cuda.get_device_properties(
+               device).multi_processor_count).as_dict()}
+    impls = [("", ours)] + ([("cublas_", cublas_fn)] if cublas else [])
+    for prefix, fn in impls:
+        for i in range(3):
+            fn(sets[i % n_sets], stream)
+        lat = per_launch_latency(fn, sets, lat_n)
+        _, chunks = graph_chunks(fn, sets, graph_steps, 3)
+        med, _, _ = chunk_stats(chunks)
+        out[prefix + "median_us"] = round(statistics.median(lat) * 1e3, 3)
+        out[prefix + "graph_us"] = round(med * 1e3, 3)
+    out["frac"] = round(algo_bytes(m, k, n) / (out["graph_us"] * 1e-6) / 1e9 / peak, 4)
+    if cublas:
+        out["speedup_median"] = round(out["cublas_median_us"] / out["median_us"], 4)
+        out["speedup_graph"] = round(out["cublas_graph_us"] / out["graph_us"], 4)
+    if tinym_b200.device_status():
+        raise SystemExit(f"device error word set at point ({m},{k},{n})")
+    del sets
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_sweep(args, device):
+    """M = 1..16 over the three (K, N) pairs, W from
+    Uniform(-1,1) and Student-t(3), ours and cuBLASLt, one JSON line per
+    point on stdout."""
+    import torch
+
+    import candidate_kernel
+
+    candidate_kernel.build()
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    peak = float(measured_peaks().get("hbm_gbs") or FALLBACK_HBM_GBS)
+    dists = args.sweep_dists.split(",")
+    for (k, n) in ((6144, 5120), (5120, 8192), (5120, 16384)):
+        for m in range(1, 17):
+            for d in dists:
+                p = measure_point(m, k, n, device, l2, peak, w_dist=d, lat_n=40, graph_steps=60,
+                                  seed=m * 1000 + n)
+                print(json.dumps(p), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200000)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
@@ -403,16 +522,22 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cublas", action="store_true")
     ap.add_argument("--no-act", action="store_true", help="skip the fused activation path")
+    ap.add_argument("--no-points", action="store_true",
+                    help="1 GPU: skip the six official points beside the workload")
     ap.add_argument("--no-fused-gather", action="store_true",
                     help="N > 1: skip the fused all-gather comparison")
     ap.add_argument("--plan", default=None,
                     help="explicit TC plan 'split,stages,block_k,tile_m' instead of the "
                          "dispatch table (re-measures one point of a plan sweep)")
-    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
-                    help="N > 1: weak = every rank owns a full workload-N slab of a GEMM "
-                         "whose N grows with the rank count (value); strong = the "
-                         "workload's N split over the ranks (also reported beside a weak "
-                         "value as strong_scaling)")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="strong",
+                    help="N > 1: strong = the workload's N split over the ranks (value; "
+                         "the fixed problem's N-sharded speed-up); weak = every rank owns a "
+                         "full workload-N slab (reported beside a strong value as "
+                         "weak_scaling)")
+    ap.add_argument("--sweep", action="store_true",
+                    help="time M = 1..16 over the three (K, N) pairs (ours and cuBLASLt), "
+                         "one JSON line per point, instead of the bench line")
+    ap.add_argument("--sweep-dists", default="uniform,student_t")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     m, k, n = WORKLOADS[args.workload]
@@ -428,6 +553,11 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
+    if args.sweep:
+        if world != 1:
+            raise SystemExit("--sweep runs on one GPU")
+        run_sweep(args, device)
+        return
     dist = None
     if world > 1:
         import datetime
@@ -458,11 +588,21 @@ def main():
         explicit = tinym_b200.check_plan(m, n_local, k, tinym_b200.make_plan(
             tinym_b200.KERNEL_TC, sp, st, 8 if m <= 8 else 16, block_k=bk, tile_m=tm))
         plan = explicit
+    peaks = measured_peaks()
+    peak = peaks.get("hbm_gbs")
+    peak_note = "measured" if peak else "fallback"
+    peak = float(peak or FALLBACK_HBM_GBS)
 
     def ours(s, stream_handle):
         x, w, y, sx, sw, alpha = s
         tinym_b200.gemm_ptr(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n_local, k,
                             alpha_ptr=alpha.data_ptr(), plan=explicit, stream=stream_handle)
+
+    def max_over_ranks(*vals):
+        t = torch.tensor(list(vals), device=device, dtype=torch.float64)
+        if dist is not None:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return [float(v) for v in t.tolist()]
 
     # ---- cold-L2 per-launch latency (spacer protocol), untimed for `value`
     for i in range(args.warmup):
@@ -471,18 +611,24 @@ def main():
     per = per_launch_latency(ours, sets, lat_n)
     median_us = statistics.median(per) * 1e3
 
-    # ---- timed region: exactly K steps, barrier + synchronize on both sides
+    # ---- timed region: exactly K steps as a few back-to-back graph replays,
+    # barrier + synchronize on both sides; the step time is the median over
+    # the replays (max over ranks)
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local_rank) as clk:
-        span = graph_throughput(ours, sets, args.steps, args.warmup)
+        span, chunks = graph_chunks(ours, sets, args.steps, args.warmup)
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
     err = tinym_b200.device_status()
     if err:
         raise SystemExit(f"device error word 0x{err:x} after the timed loop")
+    med_ms, p10_ms, p90_ms = chunk_stats(chunks)
+    med_ms, p10_ms, p90_ms, span_max = max_over_ranks(med_ms, p10_ms, p90_ms, span)
+    value_gbs = algo_bytes(m, k, n_local) * world / (med_ms * 1e-3) / 1e9
+    step_us = med_ms * 1e3
 
     # the same back-to-back loop with TINYM_FLAG_STATIC_W (weights never
     # written by the preceding kernel: W streams during the previous GEMM's
@@ -492,48 +638,39 @@ def main():
         tinym_b200.gemm_ptr(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n_local, k,
                             alpha_ptr=alpha.data_ptr(), stream=stream_handle, static_w=True)
 
-    sw_steps = min(args.steps, 20000)
-    static_span = graph_throughput(ours_static, sets, sw_steps, args.warmup)
-    st_t = torch.tensor([static_span / sw_steps], device=device, dtype=torch.float64)
+    _, st_chunks = graph_chunks(ours_static, sets, min(args.steps, 2000), args.warmup)
+    static_us = max_over_ranks(chunk_stats(st_chunks)[0])[0] * 1e3
+
+    # Beside the value: the other scaling mode at the same rank count.  For a
+    # strong value, weak_scaling gives every rank a full workload-N slab
+    # (per-GPU work fixed); for a weak value, strong_scaling splits N.
+    side = None
     if dist is not None:
-        dist.all_reduce(st_t, op=dist.ReduceOp.MAX)
-    static_us = float(st_t.item()) * 1e3
+        other = "weak" if args.scaling == "strong" else "strong"
+        try:
+            n_s, n_s_total = rank_slab(n, world, other)
+        except ValueError:
+            n_s = None
+        if n_s is not None:
+            ss_sets = make_operands(m, k, n_s, max(2, math.ceil(2.5 * l2 / (n_s * k + m * k)) + 1),
+                                    device, seed=101 + rank)
 
-    span_t = torch.tensor([span], device=device, dtype=torch.float64)
-    if dist is not None:
-        dist.all_reduce(span_t, op=dist.ReduceOp.MAX)
-    span_max = float(span_t.item())
-    total_bytes = algo_bytes(m, k, n_local) * world * args.steps
-    value_gbs = total_bytes / (span_max * 1e-3) / 1e9
-    mean_us = span_max / args.steps * 1e3  # average launch duration in the timed region
+            def ours_side(s, stream_handle):
+                x, w, y, sx, sw, alpha = s
+                tinym_b200.gemm_ptr(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n_s, k,
+                                    alpha_ptr=alpha.data_ptr(), stream=stream_handle)
 
-    # Beside a weak-scaling value: the N-sharded latency of the fixed
-    # problem (the workload's N split over the ranks), back-to-back, max over
-    # ranks -- how far one GEMM of this size speeds up on more GPUs.
-    strong = None
-    if dist is not None and args.scaling == "weak" and n % world == 0:
-        n_s = n // world
-        ss_sets = make_operands(m, k, n_s, max(2, math.ceil(2.5 * l2 / (n_s * k + m * k)) + 1),
-                                device, seed=101 + rank)
-
-        def ours_strong(s, stream_handle):
-            x, w, y, sx, sw, alpha = s
-            tinym_b200.gemm_ptr(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n_s, k,
-                                alpha_ptr=alpha.data_ptr(), stream=stream_handle)
-
-        s_steps = min(args.steps, 20000)
-        torch.cuda.synchronize()
-        dist.barrier()
-        s_span = graph_throughput(ours_strong, ss_sets, s_steps, args.warmup)
-        s_t = torch.tensor([s_span / s_steps], device=device, dtype=torch.float64)
-        dist.all_reduce(s_t, op=dist.ReduceOp.MAX)
-        s_us = float(s_t.item()) * 1e3
-        strong = {"N": n, "n_per_gpu": n_s, "us_per_launch": round(s_us, 3),
-                  "aggregate_gbs": round(algo_bytes(m, k, n_s) * world / (s_us * 1e-6) / 1e9, 1),
-                  "plan": tinym_b200.select_plan(m, n_s, k, sm_count).as_dict(),
-                  "protocol": "CUDA-graph back-to-back launches, cold W (rotating buffers), "
-                              "max over ranks"}
-        del ss_sets
+            torch.cuda.synchronize()
+            dist.barrier()
+            _, s_chunks = graph_chunks(ours_side, ss_sets, min(args.steps, 2000), args.warmup)
+            s_us = max_over_ranks(chunk_stats(s_chunks)[0])[0] * 1e3
+            side = (f"{other}_scaling",
+                    {"N": n_s_total, "n_per_gpu": n_s, "us_per_launch": round(s_us, 3),
+                     "aggregate_gbs": round(algo_bytes(m, k, n_s) * world / (s_us * 1e-6) / 1e9, 1),
+                     "plan": tinym_b200.select_plan(m, n_s, k, sm_count).as_dict(),
+                     "protocol": "median over CUDA-graph replays of back-to-back launches, "
+                                 "cold W (rotating buffers), max over ranks"})
+            del ss_sets
 
     # optional all-gather of Y (timed separately)
     allgather_us = None
@@ -549,16 +686,14 @@ def main():
             dist.all_gather_into_tensor(y_full, y_loc)
         evs[1].record()
         torch.cuda.synchronize()
-        t = torch.tensor([evs[0].elapsed_time(evs[1]) / 50 * 1e3], device=device,
-                         dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        allgather_us = float(t.item())
+        allgather_us = max_over_ranks(evs[0].elapsed_time(evs[1]) / 50 * 1e3)[0]
 
     # GEMM + gather of Y on every rank, two ways, per call on the device
     # (a spacer covers the host's enqueueing; max over ranks): NCCL
     # all-gather after the GEMM, and the gather fused into the GEMM's
     # epilogue (peer stores + arrival counters, tinym_fp8_gemm_allgather).
     gather_cmp = None
+    gather_check = None
     e2e_dist = None
     if dist is not None and not args.no_fused_gather:
         from tinym_b200.sharded import ShardedFp8Gemm
@@ -577,10 +712,7 @@ def main():
                 step(i)
             e1.record()
             torch.cuda.synchronize()
-            tt = torch.tensor([e0.elapsed_time(e1) / iters * 1e3], device=device,
-                              dtype=torch.float64)
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            return float(tt.item())
+            return max_over_ranks(e0.elapsed_time(e1) / iters * 1e3)[0]
 
         gather_cmp = {"protocol": f"{iters} back-to-back calls after a spacer, cold W "
                                   "(rotating slabs), device time, max over ranks"}
@@ -601,14 +733,12 @@ def main():
 
             gather_cmp["gemm_fused_allgather_us"] = round(device_time(fused_step), 3)
             # every rank takes the same branch: the error word's max over ranks
-            ew = torch.tensor([tinym_b200.device_status()], device=device, dtype=torch.int64)
-            dist.all_reduce(ew, op=dist.ReduceOp.MAX)
-            err_word = int(ew.item())
+            err_word = int(max_over_ranks(float(tinym_b200.device_status()))[0])
             if err_word:
                 gather_cmp["error"] = f"device error word 0x{err_word:x}"
             elif args.e2e_steps > 0:
                 # End to end at N GPUs through the public API: every step each
-                # rank copies its X and W slab from pinned host memory, runs
+                # rank copies X and its W slab from pinned host memory, runs
                 # the sharded GEMM with the fused gather, and reads the full
                 # Y back to the host.
                 x0, w0, _, _, _, a0 = sets[0]
@@ -637,10 +767,7 @@ def main():
                     e2e_dist_step()
                 e1.record()
                 torch.cuda.synchronize()
-                tt = torch.tensor([e0.elapsed_time(e1) / args.e2e_steps], device=device,
-                                  dtype=torch.float64)
-                dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-                e2e_ms = float(tt.item())
+                e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.e2e_steps)[0]
                 e2e_dist = {"value": round(algo_bytes(m, k, n_total) / (e2e_ms * 1e-3) / 1e9, 3),
                             "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
                             "h2d_bytes_per_step": int(hx.numel() + hw.numel()),
@@ -650,19 +777,16 @@ def main():
             g.close_fused_gather()
         except Exception as e:  # reported, not fatal to the main measurement
             gather_cmp["error"] = f"{type(e).__name__}: {e}"
+        gather_check = check_fused_gather(m, k, n_total, device, dist, max_over_ranks)
 
     out = None
     if rank == 0:
-        peaks = measured_peaks()
-        peak = peaks.get("hbm_gbs")
-        peak_note = "measured" if peak else "fallback"
-        peak = float(peak or FALLBACK_HBM_GBS)
-        achieved = algo_bytes(m, k, n_local) / (mean_us * 1e-6) / 1e9
+        achieved = algo_bytes(m, k, n_local) / (step_us * 1e-6) / 1e9
         out = {
             "metric": f"achieved HBM GB/s, cold-L2 FP8 GEMM (M={m},K={k},N={n})",
             "value": round(value_gbs, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(span_max / args.steps, 6),
+            "ms_per_step": round(med_ms, 6),
             "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
             "dtype": "e4m3 in / f32 acc / bf16 out", "data": "synthetic",
             "config": {"workload": args.workload, "M": m, "K": k, "N": n_total, "n_per_gpu": n_local,
@@ -672,19 +796,24 @@ def main():
                                   f"({n_sets * set_bytes / 2**20:.0f} MiB > 2x L2 "
                                   f"{l2 / 2**20:.0f} MiB)",
                        "plan": plan.as_dict()},
+            "timing": {"statistic": "median over CUDA-graph replays of back-to-back launches "
+                                    "(the K timed steps cut into a few replays, queued behind "
+                                    "a spin spacer, an event between replays)",
+                       "replays": len(chunks), "launches_per_replay": max(sz for sz, _ in chunks),
+                       "p10_us": round(p10_ms * 1e3, 3), "p90_us": round(p90_ms * 1e3, 3),
+                       "mean_us": round(span_max / args.steps * 1e3, 3)},
             "median_us": round(median_us, 3),
             "p10_us": round(sorted(per)[len(per) // 10] * 1e3, 3),
             "p90_us": round(sorted(per)[(9 * len(per)) // 10] * 1e3, 3),
             "latency_protocol": f"{lat_n} single launches, each after a GPU spin spacer, "
                                 "rotating buffers (cold W), CUDA events",
-            "graph_us_per_launch": round(mean_us, 3),
+            "graph_us_per_launch": round(step_us, 3),
             "graph_us_per_launch_static_w": round(static_us, 3),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_source": f"{peak_note} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
-                         # ncu captures are of the workload's 1-GPU launch: it
-                         # applies to every rank of a weak-scaling run (same
-                         # slab), to no rank of a strong-scaling one
+                         # ncu captures are of the workload's 1-GPU launch: they
+                         # apply to a rank whose slab is the whole workload
                          "traffic": committed_traffic(args.workload) if n_local == n else None,
                          "algorithmic_bytes_per_launch": algo_bytes(m, k, n_local)},
             "gpu_launches": args.steps,
@@ -694,10 +823,12 @@ def main():
             out["allgather_us"] = round(allgather_us, 2)
         if gather_cmp is not None:
             out["gather_of_y"] = gather_cmp
+        if gather_check is not None:
+            out["gather_check"] = gather_check
         if e2e_dist is not None:
             out["e2e"] = e2e_dist
-        if strong is not None:
-            out["strong_scaling"] = strong
+        if side is not None:
+            out[side[0]] = side[1]
 
     # ---- cuBLASLt competitor (1 GPU only, same buffers / protocol)
     if rank == 0 and world == 1 and not args.no_cublas:
@@ -710,8 +841,8 @@ def main():
         per_cb = per_launch_latency(cublas, sets, lat_n)
         out["cublas_median_us"] = round(statistics.median(per_cb) * 1e3, 3)
         out["speedup_vs_cublas"] = round(out["cublas_median_us"] / median_us, 4)
-        cb_span = graph_throughput(cublas, sets, min(args.steps, 4000), args.warmup)
-        out["cublas_graph_us_per_launch"] = round(cb_span / min(args.steps, 4000) * 1e3, 3)
+        _, cb_chunks = graph_chunks(cublas, sets, min(args.steps, 2000), args.warmup)
+        out["cublas_graph_us_per_launch"] = round(chunk_stats(cb_chunks)[0] * 1e3, 3)
         # the reference harness's own protocol (256 MiB memset before each
         # launch, events around the call; triton's do_bench, which the
         # harness calls, returns the mean, its fallback the median)
@@ -750,8 +881,7 @@ def main():
         for i in range(args.warmup):
             act(sets[i % n_sets], stream.cuda_stream)
         per_act = per_launch_latency(act, sets, min(lat_n, 1000))
-        a_steps = min(args.steps, 4000)
-        act_span = graph_throughput(act, sets, a_steps, args.warmup)
+        _, act_chunks = graph_chunks(act, sets, min(args.steps, 2000), args.warmup)
         # the unfused alternative: torch's own per-tensor quantisation
         # (the harness's quantize_per_tensor ops, fp8_gemm_task_harness.py:41-44)
         # followed by our GEMM
@@ -771,9 +901,9 @@ def main():
         out["act_quant_gemm"] = {
             "input": "bf16 X, per-tensor E4M3 quantisation on the device + GEMM (2 kernels, PDL)",
             "median_us": round(statistics.median(per_act) * 1e3, 3),
-            "graph_us_per_call": round(act_span / a_steps * 1e3, 3),
+            "graph_us_per_call": round(chunk_stats(act_chunks)[0] * 1e3, 3),
             "plain_gemm_median_us": round(median_us, 3),
-            "plain_gemm_graph_us": round(mean_us, 3),
+            "plain_gemm_graph_us": round(step_us, 3),
             "unfused_torch_quantise_then_gemm_median_us":
                 round(statistics.median(per_unf) * 1e3, 3)}
         if tinym_b200.device_status():
@@ -814,14 +944,64 @@ def main():
                           "api": "candidate_kernel.fp8_gemm",
                           "host_buffers": host.describe()}
         out["gpu_launches"] = args.steps  # timed region only (one launch per step)
-        if not args.no_cpu_baseline:
-            out["cpu_baseline"] = cpu_baseline(m, k, n, budget_s=args.cpu_budget)
+
+    # ---- the six official points beside the workload (1 GPU, same protocols)
+    if rank == 0 and world == 1 and not args.no_points:
+        del sets
+        torch.cuda.empty_cache()
+        pts = {}
+        for (pm, pk, pn) in OFFICIAL_POINTS:
+            pts[f"m{pm}_k{pk}_n{pn}"] = measure_point(pm, pk, pn, device, l2, peak,
+                                                      cublas=not args.no_cublas,
+                                                      seed=pm + pk + pn)
+        out["points"] = pts
+
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(m, k, n, budget_s=args.cpu_budget)
 
     if rank == 0:
         print(json.dumps(out), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def check_fused_gather(m, k, n, device, dist, max_over_ranks):
+    """One call of the public N-sharded API with the fused gather
+    (ShardedFp8Gemm.from_full_weight + fused) on seeded data that every rank
+    draws identically, outside any timed region.  Each rank compares its
+    gathered Y[M, N] with the FP32 reference of the whole problem,
+    (X.float() @ W.float().T) * alpha (fp8_gemm_task_harness.py:63-65),
+    computed by torch on the device: max harness-relative error
+    (max |y - ref| / max(|ref|, 1), :72-73) and elements above 0.02.
+    Returns the worst over ranks."""
+    import torch
+
+    from tinym_b200.sharded import ShardedFp8Gemm
+
+    (x, w, _, _, _, alpha), = make_operands(m, k, n, 1, device, seed=4242)
+    try:
+        g = ShardedFp8Gemm.from_full_weight(w)
+        g.enable_fused_gather(m_max=m, device=device)
+        y = g.fused(x, alpha).float()
+        ref = (x.float() @ w.float().t()) * alpha
+        rel = (y - ref).abs() / ref.abs().clamp(min=1.0)
+        max_rel, bad = float(rel.max().item()), float((rel > 0.02).sum().item())
+        torch.cuda.synchronize()
+        g.close_fused_gather()
+        err = "none"
+    except Exception as e:  # every rank still joins the reductions below
+        max_rel, bad, err = float("inf"), float("inf"), f"{type(e).__name__}: {e}"
+    max_rel, bad = max_over_ranks(max_rel, bad)
+    out = {"max_rel": max_rel if math.isfinite(max_rel) else None,
+           "mismatches_0p02": int(bad) if math.isfinite(bad) else None,
+           "tolerance": "max_rel <= 4e-3 and no element above 0.02 (BASELINE.json)",
+           "reference": "torch FP32 (X.float() @ W.float().T) * alpha on the device",
+           "api": "ShardedFp8Gemm.from_full_weight + enable_fused_gather + fused"}
+    out["ok"] = bool(max_rel <= 4e-3 and bad == 0)
+    if err != "none":
+        out["error"] = err
+    return out
 
 
 if __name__ == "__main__":

@@ -28,7 +28,10 @@
  *   - X and W must be 16-byte aligned; Y must be 2-byte aligned.
  *   - Inputs are borrowed; nothing is retained after the call returns
  *     except cached TMA descriptors keyed by (pointer, shape).
- *   - The library allocates no device memory on the call path.
+ *   - The library allocates no device memory on the call path.  The first
+ *     GEMM call on a device allocates one pinned, device-mapped 4-byte host
+ *     word (the pending-error word, see tinym_pending_errors); the
+ *     no-allocation entry point never does.
  */
 #ifndef TINYM_B200_H
 #define TINYM_B200_H
@@ -40,7 +43,7 @@
 extern "C" {
 #endif
 
-#define TINYM_ABI_VERSION 6
+#define TINYM_ABI_VERSION 7
 
 /* Exported-symbol marker (the library is built with hidden visibility). */
 #if defined(__GNUC__)
@@ -152,6 +155,18 @@ TINYM_API int tinym_plan_max_active_clusters(int64_t m, int64_t n, int64_t k,
  * forever, include/fp8_gemm_tinym.cuh:164-176). */
 TINYM_API int tinym_device_status(uint32_t* flags, int32_t clear);
 
+/* Pending errors of the current device, without synchronising: the bits of
+ * bounded waits that ran out in kernels that have already finished (0 =
+ * none), read from a pinned host word that those kernels write at system
+ * scope.  Returns TINYM_ERR_DEVICE_TIMEOUT when any bit is set; clear != 0
+ * resets the word.  A caller checks it before each launch so that the
+ * unspecified output of a timed-out GEMM is reported at the next call (the
+ * torch ops raise RuntimeError) instead of being used silently.  Reflects
+ * only kernels launched after the device's first GEMM call (which creates
+ * the word); tinym_device_status sees every kernel.  No reference
+ * counterpart (the reference's waits spin forever). */
+TINYM_API int tinym_pending_errors(uint32_t* flags, int32_t clear);
+
 /* Failure-detection self-test: launches the GEMM (plan = NULL for the
  * dispatch table's choice) with fault injection that makes the producer
  * issue no copies, so every consumer wait runs out after timeout_ns
@@ -213,13 +228,19 @@ TINYM_API int tinym_fp8_gemm_quant_act(const void* x_act, int32_t act_dtype, con
                                        int64_t m, int64_t n, int64_t k, void* workspace,
                                        const tinym_plan* plan, void* stream);
 
-/* tinym_fp8_gemm_quant_act without a caller-provided workspace: the
- * workspace is a static device array inside the library (its address found
- * per device with cudaGetSymbolAddress), so the call allocates nothing and
- * needs no workspace argument.  M * K must be at most 524288 (else
- * TINYM_ERR_UNSUPPORTED_SHAPE).  The array is shared by every call on a
- * device: calls must be ordered on one stream (or otherwise serialised);
- * x_scale and alpha can be read back only until the next such call. */
+/* tinym_fp8_gemm_quant_act without a caller-provided workspace, for callers
+ * that cannot allocate device memory (an allocator-less runtime, a caller
+ * inside a memory pool it does not own).  No counterpart in the reference.
+ * The workspace is a static device array inside the library (its address
+ * found per device with cudaGetSymbolAddress on the device's first such
+ * call, which should therefore come before any stream capture), so the call
+ * allocates nothing and needs no workspace argument.  M * K must be at most
+ * 524288 (else TINYM_ERR_UNSUPPORTED_SHAPE).  The array is shared by every
+ * call on a device and keeps the last call's contents: calls must be
+ * ordered on one stream (or otherwise serialised), since calls that overlap
+ * on the GPU race.  x_scale and alpha are not observable in this form.  The
+ * cached address assumes the device's primary context and no
+ * cudaDeviceReset while the library is loaded. */
 TINYM_API int tinym_fp8_gemm_quant_act_noalloc(const void* x_act, int32_t act_dtype,
                                                const void* w, const float* w_scale_dev,
                                                void* y, int64_t ldy, int64_t m, int64_t n,

@@ -108,6 +108,12 @@ struct DeviceInfo {
     int sm_count = 0;
     int cc_major = 0, cc_minor = 0;
     std::atomic<uint32_t> attr_done{0};  // bit per kernel instance: smem attribute set
+    // Pending-error word: one pinned, device-mapped host word per device.
+    // Kernels whose bounded waits run out OR their bit into it (system
+    // scope), so the host sees a timeout at its next call without
+    // synchronising.  Allocated on the first GEMM call of the device.
+    std::atomic<volatile uint32_t*> err_host{nullptr};
+    uint32_t* err_host_dev = nullptr;
 };
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_dev_mu;
@@ -133,6 +139,34 @@ int device_info(int dev, DeviceInfo** out) {
                     "device %d is sm_%d%d; this library is built for sm_100a (B200)", dev,
                     d.cc_major, d.cc_minor);
     *out = &d;
+    return TINYM_OK;
+}
+
+// The device's pending-error word: its device address in *dev_ptr (null
+// when allocate is false and the word does not exist yet).
+int pending_word(DeviceInfo* d, bool allocate, uint32_t** dev_ptr) {
+    *dev_ptr = nullptr;
+    if (d->err_host.load(std::memory_order_acquire)) {
+        *dev_ptr = d->err_host_dev;
+        return TINYM_OK;
+    }
+    if (!allocate) return TINYM_OK;
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (!d->err_host.load(std::memory_order_relaxed)) {
+        void* h = nullptr;
+        cudaError_t e = cudaHostAlloc(&h, sizeof(uint32_t), cudaHostAllocMapped | cudaHostAllocPortable);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaHostAlloc(pending-error word)");
+        *static_cast<volatile uint32_t*>(h) = 0u;
+        void* dp = nullptr;
+        e = cudaHostGetDevicePointer(&dp, h, 0);
+        if (e != cudaSuccess) {
+            cudaFreeHost(h);
+            return cuda_fail(e, "cudaHostGetDevicePointer(pending-error word)");
+        }
+        d->err_host_dev = static_cast<uint32_t*>(dp);
+        d->err_host.store(static_cast<volatile uint32_t*>(h), std::memory_order_release);
+    }
+    *dev_ptr = d->err_host_dev;
     return TINYM_OK;
 }
 
@@ -575,10 +609,12 @@ struct GemmLaunch {
     const void* fn;
 };
 
+// may_allocate = false: use the device's pending-error word only if an
+// earlier call has already allocated it (the no-allocation entry point).
 static int gemm_prepare(const void* x, const void* w, void* y, int64_t ldy, int64_t m, int64_t n,
                         int64_t k, const float* alpha_dev, float alpha, const tinym_plan* plan,
                         uint32_t flags, uint64_t timeout_ns, bool w_packed,
-                        const tinym_gather_desc* gd, GemmLaunch* out) {
+                        const tinym_gather_desc* gd, GemmLaunch* out, bool may_allocate = true) {
     if (!x || !w || !y) return fail(TINYM_ERR_INVALID_ARGUMENT, "X, W and Y must be non-null");
     int st = check_shape(m, n, k);
     if (st != TINYM_OK) return st;
@@ -652,6 +688,7 @@ static int gemm_prepare(const void* x, const void* w, void* y, int64_t ldy, int6
     prm.flags = flags & 0xFFFFu;  // the kernel's kFlag* bits only
     prm.timeout_ns = timeout_ns;
     prm.w_packed_kc = w_packed ? static_cast<int32_t>(tinym::packed_chunks(k)) : 0;
+    if ((st = pending_word(di, may_allocate, &prm.err_host)) != TINYM_OK) return st;
     if (gd) {
         // CTA (0,0) waits for the other ranks: the whole grid must be resident
         // at once, or a waiting CTA could hold an SM another CTA needs.
@@ -738,11 +775,10 @@ int tinym_quant_workspace_bytes(int64_t m, int64_t k, int64_t* bytes) {
     return TINYM_OK;
 }
 
-int tinym_fp8_gemm_quant_act(const void* x_act, int32_t act_dtype, const void* w,
-                             const float* w_scale_dev, void* y, int64_t ldy, int64_t m,
-                             int64_t n, int64_t k, void* workspace, const tinym_plan* plan,
-                             void* stream) {
-    t_last_error[0] = '\0';
+static int quant_act_impl(const void* x_act, int32_t act_dtype, const void* w,
+                          const float* w_scale_dev, void* y, int64_t ldy, int64_t m, int64_t n,
+                          int64_t k, void* workspace, const tinym_plan* plan, void* stream,
+                          bool may_allocate) {
     if (!x_act || !w || !w_scale_dev || !y || !workspace)
         return fail(TINYM_ERR_INVALID_ARGUMENT, "X, W, w_scale, Y and workspace must be non-null");
     if (act_dtype != TINYM_ACT_BF16 && act_dtype != TINYM_ACT_F32)
@@ -761,11 +797,14 @@ int tinym_fp8_gemm_quant_act(const void* x_act, int32_t act_dtype, const void* w
     if ((st = gemm_prepare(ws + tinym::kQuantWsHeader, w, y, ldy, m, n, k,
                            reinterpret_cast<const float*>(ws) + 1, 0.0f, plan,
                            tinym::kFlagEarlyW | kFlagQuantPrologue, kDefaultTimeoutNs, false,
-                           nullptr, &g)) != TINYM_OK)
+                           nullptr, &g, may_allocate)) != TINYM_OK)
         return st;
     // Ordinary stream order (no programmatic attribute): everything before
     // this kernel has completed when it starts, which is what lets the GEMM
-    // read W ahead of its griddepcontrol.wait.
+    // read W ahead of its griddepcontrol.wait.  It must stay that way for
+    // the no-allocation form too: its static workspace is rewritten by this
+    // kernel, so the previous call's GEMM (launched with the programmatic
+    // attribute, reading the workspace) must have completed first.
     auto s = static_cast<cudaStream_t>(stream);
     if (act_dtype == TINYM_ACT_BF16)
         tinym::tinym_quant_act_kernel<__nv_bfloat16>
@@ -777,6 +816,15 @@ int tinym_fp8_gemm_quant_act(const void* x_act, int32_t act_dtype, const void* w
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "quantise kernel launch");
     return gemm_launch(g, stream);
+}
+
+int tinym_fp8_gemm_quant_act(const void* x_act, int32_t act_dtype, const void* w,
+                             const float* w_scale_dev, void* y, int64_t ldy, int64_t m,
+                             int64_t n, int64_t k, void* workspace, const tinym_plan* plan,
+                             void* stream) {
+    t_last_error[0] = '\0';
+    return quant_act_impl(x_act, act_dtype, w, w_scale_dev, y, ldy, m, n, k, workspace, plan,
+                          stream, true);
 }
 
 int tinym_fp8_gemm_quant_act_noalloc(const void* x_act, int32_t act_dtype, const void* w,
@@ -795,8 +843,8 @@ int tinym_fp8_gemm_quant_act_noalloc(const void* x_act, int32_t act_dtype, const
     if (dev < 0 || dev >= kMaxDevices) return fail(TINYM_ERR_CUDA, "device ordinal %d out of range", dev);
     void* ws = nullptr;
     if ((st = scratch_address(dev, &ws)) != TINYM_OK) return st;
-    return tinym_fp8_gemm_quant_act(x_act, act_dtype, w, w_scale_dev, y, ldy, m, n, k, ws, plan,
-                                    stream);
+    return quant_act_impl(x_act, act_dtype, w, w_scale_dev, y, ldy, m, n, k, ws, plan, stream,
+                          false);
 }
 
 int tinym_ipc_export(const void* ptr, void* handle, int64_t* offset) {
@@ -944,7 +992,38 @@ int tinym_device_status(uint32_t* flags, int32_t clear) {
         e = cudaMemcpyToSymbol(tinym::g_err_word, &zero, sizeof(uint32_t));
         if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyToSymbol(error word)");
     }
+    // The same bits were also posted to the pending-error word (if the
+    // device has one); after a synchronising read both are consumed.
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices) {
+        volatile uint32_t* h = g_dev[dev].err_host.load(std::memory_order_acquire);
+        if (h) {
+            uint32_t* word = const_cast<uint32_t*>(h);
+            *flags |= clear ? __atomic_exchange_n(word, 0u, __ATOMIC_ACQ_REL)
+                            : __atomic_load_n(word, __ATOMIC_ACQUIRE);
+        }
+    }
     return *flags ? fail(TINYM_ERR_DEVICE_TIMEOUT, "device error word 0x%x", *flags) : TINYM_OK;
+}
+
+int tinym_pending_errors(uint32_t* flags, int32_t clear) {
+    t_last_error[0] = '\0';
+    if (!flags) return fail(TINYM_ERR_INVALID_ARGUMENT, "flags is NULL");
+    *flags = 0u;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= kMaxDevices) return fail(TINYM_ERR_CUDA, "device ordinal %d out of range", dev);
+    volatile uint32_t* h = g_dev[dev].err_host.load(std::memory_order_acquire);
+    if (h) {
+        uint32_t* word = const_cast<uint32_t*>(h);
+        *flags = clear ? __atomic_exchange_n(word, 0u, __ATOMIC_ACQ_REL)
+                       : __atomic_load_n(word, __ATOMIC_ACQUIRE);
+    }
+    return *flags ? fail(TINYM_ERR_DEVICE_TIMEOUT,
+                         "a kernel that finished earlier on device %d ran out of a bounded wait "
+                         "(error bits 0x%x): its output is unspecified", dev, *flags)
+                  : TINYM_OK;
 }
 
 }  // extern "C"

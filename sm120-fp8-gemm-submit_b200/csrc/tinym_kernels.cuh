@@ -93,6 +93,10 @@ struct TinymParams {
     unsigned long long gather_target;
     __nv_bfloat16* peer_y[8];
     unsigned long long* peer_flag[8];
+    // Host-mapped pending-error word (device address), or null: a wait that
+    // runs out also sets its bit here, where the host can see it at the next
+    // call without synchronising the device.
+    uint32_t* err_host;
 };
 constexpr int kMaxPeers = 8;
 
@@ -248,7 +252,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // bounded waits run out and report through the error word.
     const int n_issue = (p.flags & kFlagInjectNoLoads) ? 0 : nkb;
 
-    const WaitGuard guard{abort_flag, &g_err_word, p.timeout_ns};
+    const WaitGuard guard{abort_flag, &g_err_word, p.timeout_ns, p.err_host};
 
     // The producer thread initialises the barriers and immediately puts the
     // first ring-full of loads in flight, so the DRAM latency of the first
@@ -523,7 +527,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         const uint64_t t0 = globaltimer_ns();
                         while (ld_acquire_sys_u64(p.peer_flag[p.rank]) < p.gather_target) {
                             if (globaltimer_ns() - t0 > p.timeout_ns) {
-                                atomicOr(&g_err_word, kErrPeerWait);
+                                report_timeout(&g_err_word, p.err_host, kErrPeerWait);
                                 break;
                             }
                             __nanosleep(32);
@@ -580,7 +584,7 @@ __global__ void __launch_bounds__(32 * (CWARPS + 1), 1)
     const int nkb = kb1 - kb0;
     const int n_issue = (p.flags & kFlagInjectNoLoads) ? 0 : nkb;
 
-    const WaitGuard guard{abort_flag, &g_err_word, p.timeout_ns};
+    const WaitGuard guard{abort_flag, &g_err_word, p.timeout_ns, p.err_host};
 
     int issued = 0;
     uint64_t pol_w = 0, pol_x = 0;

@@ -91,7 +91,16 @@ struct WaitGuard {
     volatile uint32_t* abort;  // shared-memory flag
     uint32_t* err_word;        // global error word (may be null)
     uint64_t timeout_ns;
+    uint32_t* err_host;        // host-mapped pending-error word (may be null)
 };
+
+// Report a wait that ran out: the device error word, and the host-mapped
+// word that the host reads without synchronising (system scope).
+__device__ __forceinline__ void report_timeout(uint32_t* err_word, uint32_t* err_host,
+                                               uint32_t code) {
+    if (err_word) atomicOr(err_word, code);
+    if (err_host) atomicOr_system(err_host, code);
+}
 
 __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, const WaitGuard& g,
                                             uint32_t code, bool honour_abort) {
@@ -102,7 +111,7 @@ __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, const
             if (honour_abort && *g.abort) return false;
             if (globaltimer_ns() - t0 > g.timeout_ns) {
                 *g.abort = 1u;
-                if (g.err_word) atomicOr(g.err_word, code);
+                report_timeout(g.err_word, g.err_host, code);
                 return false;
             }
         }

@@ -13,7 +13,9 @@
 // activation quantised per tensor on the device, then the GEMM:
 //     sm120_fp8_gemm::run_quant_act(Tensor x, Tensor b, Tensor w_scale) -> (Tensor y, Tensor x_scale)
 // Input checks mirror check_inputs (src/torch_candidate_extension.cu:17-31)
-// and raise the same RuntimeError (TORCH_CHECK) messages; shape support is
+// and raise the same RuntimeError (TORCH_CHECK) messages; every op also
+// raises before launching if an earlier GEMM on the device ran out of a
+// bounded wait (tinym_pending_errors).  Shape support is
 // decided by the C ABI (1 <= M <= 16, K % 16 == 0) instead of the six-point
 // gate of :40-46.  Y is allocated by the op (as in :49-50) and the kernel is
 // launched on the current stream of A's device (:48,:57).
@@ -44,9 +46,24 @@ void raise_status(int st) {
     TORCH_CHECK(st == TINYM_OK, tinym_status_string(st), ": ", tinym_last_error());
 }
 
+// A GEMM whose bounded device wait ran out left its output unspecified; the
+// kernel posted that to the device's pending-error word, which is checked
+// (without synchronising) before every launch, so the caller gets a
+// RuntimeError here instead of using that output silently.  The word is
+// cleared, so the call after this one runs normally.  Needs the operands'
+// device current.
+void check_pending() {
+    uint32_t flags = 0;
+    const int st = tinym_pending_errors(&flags, 1);
+    TORCH_CHECK(st == TINYM_OK || st == TINYM_ERR_DEVICE_TIMEOUT, tinym_status_string(st), ": ",
+                tinym_last_error());
+    TORCH_CHECK(flags == 0u, "TINYM_ERR_DEVICE_TIMEOUT: ", tinym_last_error());
+}
+
 at::Tensor launch(const at::Tensor& a, const at::Tensor& b, const float* alpha_dev, float alpha) {
     const int64_t m = a.size(0), k = a.size(1), n = b.size(0);
     const c10::cuda::CUDAGuard guard(a.device());
+    check_pending();
     at::Tensor y = at::empty({m, n}, a.options().dtype(at::ScalarType::BFloat16));
     if (m == 0 || n == 0) return y;
     cudaStream_t stream = at::cuda::getCurrentCUDAStream(a.get_device());
@@ -106,6 +123,7 @@ at::Tensor run_packed(const at::Tensor& a, const at::Tensor& bp, int64_t n, int6
     TORCH_CHECK(alpha.get_device() == a.get_device(), "alpha must be on A's device");
     const int64_t m = a.size(0);
     const c10::cuda::CUDAGuard guard(a.device());
+    check_pending();
     at::Tensor y = at::empty({m, n}, a.options().dtype(at::ScalarType::BFloat16));
     if (m == 0 || n == 0) return y;
     raise_status(tinym_fp8_gemm_packed(a.data_ptr(), bp.data_ptr(), y.data_ptr(), n, m, n, k,
@@ -129,6 +147,7 @@ std::tuple<at::Tensor, at::Tensor> run_quant_act(const at::Tensor& x, const at::
                 "w_scale must be a one-element float32 tensor");
     const int64_t m = x.size(0), k = x.size(1), n = b.size(0);
     const c10::cuda::CUDAGuard guard(x.device());
+    check_pending();
     at::Tensor y = at::empty({m, n}, b.options().dtype(at::ScalarType::BFloat16));
     int64_t ws_bytes = 0;
     raise_status(tinym_quant_workspace_bytes(m, k, &ws_bytes));

@@ -51,6 +51,7 @@ EXPORTED = (
     "tinym_select_plan",
     "tinym_check_plan",
     "tinym_device_status",
+    "tinym_pending_errors",
     "tinym_plan_max_active_clusters",
     "tinym_selftest_wait_timeout",
     "tinym_packed_weight_bytes",
@@ -151,6 +152,8 @@ def capi() -> ctypes.CDLL:
             lib.tinym_check_plan.restype = ctypes.c_int
             lib.tinym_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int32]
             lib.tinym_device_status.restype = ctypes.c_int
+            lib.tinym_pending_errors.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int32]
+            lib.tinym_pending_errors.restype = ctypes.c_int
             lib.tinym_selftest_wait_timeout.argtypes = [vp, vp, vp, i64, i64, i64,
                                                         ctypes.POINTER(Plan), ctypes.c_uint64, vp]
             lib.tinym_selftest_wait_timeout.restype = ctypes.c_int
@@ -410,8 +413,28 @@ def device_status(clear: bool = True) -> int:
     return int(flags.value)
 
 
+def pending_errors(clear: bool = True) -> int:
+    """Bits of bounded device waits that ran out in kernels that have already
+    finished on the current device (0 = none), read without synchronising."""
+    flags = ctypes.c_uint32(0)
+    st = capi().tinym_pending_errors(ctypes.byref(flags), 1 if clear else 0)
+    if st not in (TINYM_OK, 6):
+        _check(st)
+    return int(flags.value)
+
+
+def raise_pending() -> None:
+    """Raise TinymError if an earlier GEMM on the current device timed out
+    (its output is unspecified); clears the report."""
+    flags = ctypes.c_uint32(0)
+    st = capi().tinym_pending_errors(ctypes.byref(flags), 1)
+    if st != TINYM_OK:
+        _check(st)
+
+
 def gemm(x, w, alpha, *, out=None, plan: Plan | None = None, static_w: bool = False):
-    """torch convenience wrapper over the C ABI (device alpha, current stream)."""
+    """torch convenience wrapper over the C ABI (device alpha, current stream).
+    Raises TinymError first if an earlier GEMM on the device timed out."""
     import torch
 
     if x.dtype != torch.float8_e4m3fn or w.dtype != torch.float8_e4m3fn:
@@ -421,6 +444,8 @@ def gemm(x, w, alpha, *, out=None, plan: Plan | None = None, static_w: bool = Fa
         raise ValueError("a tensor alpha must be float32 with at least one element")
     out = _check_out(out, m, n, x)
     _check_devices(x, w, alpha if isinstance(alpha, torch.Tensor) else None, out)
+    with torch.cuda.device(x.device):
+        raise_pending()
     stream = torch.cuda.current_stream(x.device).cuda_stream
     if isinstance(alpha, torch.Tensor):
         gemm_ptr(x.data_ptr(), w.data_ptr(), out.data_ptr(), m, n, k, ldy=out.stride(0),
@@ -433,7 +458,7 @@ def gemm(x, w, alpha, *, out=None, plan: Plan | None = None, static_w: bool = Fa
 
 __all__ = [
     "capi", "load_torch_op", "select_plan", "check_plan", "make_plan", "gemm_ptr", "gemm",
-    "device_status", "Plan", "TinymError", "EXPORTED", "KERNEL_TC", "KERNEL_SIMT_M1",
+    "device_status", "pending_errors", "raise_pending", "Plan", "TinymError", "EXPORTED", "KERNEL_TC", "KERNEL_SIMT_M1",
     "packed_weight_bytes", "pack_weights_ptr", "gemm_packed_ptr", "quant_workspace_bytes",
     "gemm_quant_act", "ACT_BF16", "ACT_F32", "GatherDesc", "ipc_export", "ipc_open", "ipc_close",
     "gemm_allgather_ptr",

@@ -228,9 +228,10 @@ def make_operands(m, k, n, n_sets, device, seed=0, w_dist="normal"):
 
 
 SPACER_CYCLES = 100_000  # ~50 us of GPU spin ahead of each latency sample
+SPACER_DITHER = 8_192    # up to ~4 us more, drawn per sample (see per_launch_latency)
 
 
-def per_launch_latency(fn, sets, n, flush=None):
+def per_launch_latency(fn, sets, n, flush=None, seed=0):
     """Cold-L2 latency of single launches (ms each), measured on the device.
 
     Each sample is  [spacer] -> start event -> fn(set) -> end event.  The
@@ -240,16 +241,26 @@ def per_launch_latency(fn, sets, n, flush=None):
     the reference harness's protocol (zero a 256 MiB buffer before each
     launch, fp8_gemm_task_harness.py:84-96), which also leaves L2 full of
     dirty lines that the timed launch must write back.
+
+    Event timestamps on B200 are quantised (steps of about 1 or 2 us were
+    seen), so one sample is a multiple of that step and the median snaps to
+    a step.  The spin spacer's length is dithered by a seeded random number
+    of cycles, so the phase of the timed launch against the timestamp clock
+    varies from sample to sample and the MEAN of the samples estimates the
+    latency below the step size (reported beside the median).
     """
+    import random
+
     import torch
 
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
     stream = torch.cuda.current_stream()
+    rng = random.Random(seed)
     torch.cuda.synchronize()
     for i in range(n):
         if flush is None:
-            torch.cuda._sleep(SPACER_CYCLES)
+            torch.cuda._sleep(SPACER_CYCLES + rng.randrange(SPACER_DITHER))
         else:
             flush.zero_()
         starts[i].record(stream)
@@ -478,10 +489,12 @@ def measure_point(m, k, n, device, l2, peak, *, cublas=True, w_dist="normal", la
         _, chunks = graph_chunks(fn, sets, graph_steps, 3)
         med, _, _ = chunk_stats(chunks)
         out[prefix + "median_us"] = round(statistics.median(lat) * 1e3, 3)
+        out[prefix + "mean_us"] = round(statistics.mean(lat) * 1e3, 3)
         out[prefix + "graph_us"] = round(med * 1e3, 3)
     out["frac"] = round(algo_bytes(m, k, n) / (out["graph_us"] * 1e-6) / 1e9 / peak, 4)
     if cublas:
         out["speedup_median"] = round(out["cublas_median_us"] / out["median_us"], 4)
+        out["speedup_mean"] = round(out["cublas_mean_us"] / out["mean_us"], 4)
         out["speedup_graph"] = round(out["cublas_graph_us"] / out["graph_us"], 4)
     if tinym_b200.device_status():
         raise SystemExit(f"device error word set at point ({m},{k},{n})")
@@ -803,10 +816,11 @@ def main():
                        "p10_us": round(p10_ms * 1e3, 3), "p90_us": round(p90_ms * 1e3, 3),
                        "mean_us": round(span_max / args.steps * 1e3, 3)},
             "median_us": round(median_us, 3),
+            "mean_us": round(statistics.mean(per) * 1e3, 3),
             "p10_us": round(sorted(per)[len(per) // 10] * 1e3, 3),
             "p90_us": round(sorted(per)[(9 * len(per)) // 10] * 1e3, 3),
-            "latency_protocol": f"{lat_n} single launches, each after a GPU spin spacer, "
-                                "rotating buffers (cold W), CUDA events",
+            "latency_protocol": f"{lat_n} single launches, each after a GPU spin spacer of "
+                                "dithered length, rotating buffers (cold W), CUDA events",
             "graph_us_per_launch": round(step_us, 3),
             "graph_us_per_launch_static_w": round(static_us, 3),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
@@ -840,7 +854,9 @@ def main():
             cublas(sets[i % n_sets], stream.cuda_stream)
         per_cb = per_launch_latency(cublas, sets, lat_n)
         out["cublas_median_us"] = round(statistics.median(per_cb) * 1e3, 3)
+        out["cublas_mean_us"] = round(statistics.mean(per_cb) * 1e3, 3)
         out["speedup_vs_cublas"] = round(out["cublas_median_us"] / median_us, 4)
+        out["speedup_vs_cublas_mean"] = round(out["cublas_mean_us"] / out["mean_us"], 4)
         _, cb_chunks = graph_chunks(cublas, sets, min(args.steps, 2000), args.warmup)
         out["cublas_graph_us_per_launch"] = round(chunk_stats(cb_chunks)[0] * 1e3, 3)
         # the reference harness's own protocol (256 MiB memset before each

@@ -367,34 +367,52 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            // ---------------- MMA issuer (one thread)
-            for (int i = 0; i < nkb; ++i) {
-                const int s = i % stages;
-                if (!mbar_wait(full_bar(s), (i / stages) & 1, guard, kErrMmaWait)) break;
-                if (i == 0) TINYM_TRACE(3);
-                if (i == nkb - 1) TINYM_TRACE(4);
-                tc_fence_after_sync();
+        // ---------------- MMA issuer: the whole warp runs the loop, lane 0
+        // waits for each stage, one elected lane issues its MMAs and the
+        // commit.  The shared-memory descriptors are a per-ring base plus the
+        // stage offset plus compile-time K steps (the start-address field
+        // [0,14) cannot carry: every address is below 2^18).
+        const uint32_t tmem_u = __shfl_sync(0xFFFFFFFFu, tmem_d, 0);
+        const uint64_t da0 = sw128_kmajor_desc(w_ring);
+        const uint64_t db0 = sw128_kmajor_desc(x_ring);
+        for (int i = 0; i < nkb; ++i) {
+            const int s = i % stages;
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait(full_bar(s), (i / stages) & 1, guard, kErrMmaWait);
+            if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) break;
+            if (lane == 0 && i == 0) TINYM_TRACE(3);
+            if (lane == 0 && i == nkb - 1) TINYM_TRACE(4);
+            tc_fence_after_sync();
+            const uint64_t da = da0 + static_cast<uint64_t>((s * kWStage) >> 4);
+            const uint64_t db = db0 + static_cast<uint64_t>((s * kXStageBytes) >> 4);
+            const uint32_t acc0 = i > 0 ? 1u : 0u;  // the CTA's first MMA overwrites D
+            if (elect_one()) {
 #pragma unroll
                 for (int c = 0; c < CHUNKS; ++c) {
-                    const uint32_t a0 = w_ring + s * kWStage + c * kWChunk;
-                    const uint32_t b0 = x_ring + s * kXStageBytes + c * kXChunkBytes;
 #pragma unroll
                     for (int kk = 0; kk < kBlockK / 32; ++kk) {
-                        umma_e4m3(tmem_d, sw128_kmajor_desc(a0 + kk * 32),
-                                  sw128_kmajor_desc(b0 + kk * 32), kIdesc,
-                                  (i > 0 || c > 0 || kk > 0) ? 1u : 0u);
+                        umma_e4m3(tmem_u, da + static_cast<uint64_t>((c * kWChunk + kk * 32) >> 4),
+                                  db + static_cast<uint64_t>((c * kXChunkBytes + kk * 32) >> 4),
+                                  kIdesc, (c | kk) ? 1u : acc0);
                     }
                 }
                 umma_commit(empty_bar(s));  // frees the slot once these MMAs retire
             }
+            __syncwarp();
+        }
+        if (lane == 0) {
             umma_commit(acc_bar);  // accumulator complete (or all issued MMAs retired)
             if (*abort_flag) mbar_drain(acc_bar, 0, guard, kErrDrain);
         }
     } else {
         // ---------------- epilogue warps 2..5: TMEM lanes 32*(warp%4) ..
         grid_dependency_wait();  // alpha may be written by the previous kernel
-        alpha = load_alpha(p);   // issued early: its latency hides behind the mainloop
+        // issued early (a volatile load stays ahead of the accumulator wait):
+        // its latency hides behind the mainloop
+        if (p.alpha_ptr)
+            asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(alpha) : "l"(p.alpha_ptr) : "memory");
+        else
+            alpha = p.alpha;
         // tcgen05.ld is .sync.aligned: the whole warp takes the same branch.
         const bool ready = mbar_wait(acc_bar, 0, guard, kErrEpilogueWait) && !*abort_flag;
         if (__all_sync(0xFFFFFFFFu, ready)) {

@@ -144,8 +144,11 @@ class ShardedFp8Gemm:
 
     def fused(self, x, alpha):
         """Y[M, N] on every rank with the gather fused into the GEMM.  The
-        result is a view of an internal buffer that stays valid until the
-        call after next (two buffers alternate)."""
+        result is a view of one of two internal buffers used alternately.
+        Every read of it must be stream-ordered before this rank's next
+        fused() call (queued earlier on the same stream, or waited for):
+        once this rank's next call has stored its rows, a faster peer's call
+        after that may start storing into the buffer returned here."""
         import torch
 
         from . import gemm_allgather_ptr

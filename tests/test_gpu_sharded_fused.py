@@ -3,7 +3,8 @@
 Two processes, one per GPU: each GEMM epilogue stores its rows into every
 rank's full Y through CUDA IPC peer mappings (plain stores over NVLink, no
 TMA on peer memory) and signals the per-rank arrival counters; the handles
-are exchanged over a gloo group (no NCCL).  Every rank's result must equal,
+are exchanged over a gloo group (no NCCL).  Every rank's gathered Y must
+meet the oracle bar against the FP32 oracle of the whole problem and equal,
 bit for bit, the plain single-GPU GEMM of each rank's slab, for several
 calls in a row (both buffers, growing counters).  Skipped with fewer than
 two GPUs.
@@ -48,18 +49,25 @@ def _worker(rank, world, port, shapes, errq):
             g.enable_fused_gather(m_max=16)
             for call in range(calls):
                 m = 1 + (call * 7) % m_max
-                xq, _, _, _, alpha = orc.make_case(m, k, 1, seed=100 * call + k, dist="normal")
+                xq, _, sx, _, _ = orc.make_case(m, k, 1, seed=100 * call + k, dist="normal")
+                alpha = (sx * sw).astype(np.float32).reshape(1)
                 x = torch.from_numpy(xq).to(dev).view(torch.float8_e4m3fn)
                 a = torch.from_numpy(alpha).to(dev)
                 y = g.fused(x, a).clone()
                 torch.cuda.synchronize()
+                # the gathered Y against the FP32 oracle of the whole problem
+                out = y.float().cpu().numpy()
+                ref = orc.reference(xq, wq, alpha)
+                assert orc.max_rel_err(out, ref) <= orc.MAX_REL_TOL, (rank, m, k, n, call)
+                assert orc.mismatches(out, ref) == 0, (rank, m, k, n, call)
+                # and bit for bit against the single-GPU GEMM of every slab
                 exp = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
                 for r in range(world):
                     s0, s1 = shard_bounds(n, world, r)
                     if s1 > s0:
                         exp[:, s0:s1] = tinym_b200.gemm(x, w_full[s0:s1].contiguous(), a)
                 assert torch.equal(y, exp), (rank, m, k, n, call)
-                # every rank finishes reading before anyone starts the call after next
+                # every rank has read this call's Y before anyone starts its next call
                 dist.barrier()
             assert tinym_b200.device_status() == 0
             g.close_fused_gather()
@@ -116,13 +124,14 @@ def test_fused_gather_epilogue_single_rank(cuda_device, oracle):
     import tinym_b200
 
     k, n = 2048, 1000
-    _, wq, _, _, _ = oracle.make_case(1, k, n, seed=9, dist="normal")
+    _, wq, _, sw, _ = oracle.make_case(1, k, n, seed=9, dist="normal")
     w = torch.from_numpy(wq).to(cuda_device).view(torch.float8_e4m3fn)
     y_full = torch.empty((16, n), dtype=torch.bfloat16, device=cuda_device)
     counter = torch.zeros(1, dtype=torch.int64, device=cuda_device)
     total = 0
     for call, m in enumerate((1, 9, 16, 4)):
-        xq, _, _, _, alpha = oracle.make_case(m, k, 1, seed=call, dist="normal")
+        xq, _, sx, _, _ = oracle.make_case(m, k, 1, seed=call, dist="normal")
+        alpha = (sx * sw).astype(np.float32).reshape(1)
         x = torch.from_numpy(xq).to(cuda_device).view(torch.float8_e4m3fn)
         a = torch.from_numpy(alpha).to(cuda_device)
         total += m * n
@@ -131,6 +140,10 @@ def test_fused_gather_epilogue_single_rank(cuda_device, oracle):
                                       alpha_ptr=a.data_ptr(),
                                       stream=torch.cuda.current_stream().cuda_stream)
         torch.cuda.synchronize()
+        out = y_full[:m].float().cpu().numpy()
+        ref = oracle.reference(xq, wq, alpha)
+        assert oracle.max_rel_err(out, ref) <= oracle.MAX_REL_TOL
+        assert oracle.mismatches(out, ref) == 0
         assert torch.equal(y_full[:m], tinym_b200.gemm(x, w, a))
         assert int(counter.item()) == total
     assert tinym_b200.device_status() == 0

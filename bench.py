@@ -478,10 +478,22 @@ def measure_point(m, k, n, device, l2, peak, *, cublas=True, w_dist="normal", la
         torch._scaled_mm(x, w.t(), scale_a=sx, scale_b=sw, out_dtype=torch.bfloat16)
 
     stream = torch.cuda.current_stream(device).cuda_stream
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
     out = {"M": m, "K": k, "N": n, "w_dist": w_dist,
-           "plan": tinym_b200.select_plan(m, n, k, torch.cuda.get_device_properties(
-               device).multi_processor_count).as_dict()}
+           "plan": tinym_b200.select_plan(m, n, k, sms).as_dict()}
     impls = [("", ours)] + ([("cublas_", cublas_fn)] if cublas else [])
+    if m == 1:
+        # the CUDA-core M = 1 kernel beside the tensor-core one (same grid
+        # rule as the dispatch table: the largest K split that fits the SMs)
+        simt = simt_plan(n, k, sms)
+        out["simt_plan"] = simt.as_dict()
+
+        def simt_fn(s, h):
+            x, w, y, sx, sw, alpha = s
+            tinym_b200.gemm_ptr(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k,
+                                alpha_ptr=alpha.data_ptr(), plan=simt, stream=h)
+
+        impls.append(("simt_", simt_fn))
     for prefix, fn in impls:
         for i in range(3):
             fn(sets[i % n_sets], stream)
@@ -501,6 +513,24 @@ def measure_point(m, k, n, device, l2, peak, *, cublas=True, w_dist="normal", la
     del sets
     torch.cuda.empty_cache()
     return out
+
+
+def simt_plan(n, k, sms, stages=8, cwarps=8):
+    """A CUDA-core M = 1 plan: 128-row tiles, the largest K split (cluster
+    <= 8) that keeps tiles * split within the SMs and gives every CTA >= 2
+    stages of 128 B of K, an 8-stage ring (128 KiB of W in flight)."""
+    import tinym_b200
+
+    tiles = -(-n // 128)
+    kb = -(-k // 128)
+    split = 1
+    for sp in range(2, 9):
+        per = -(-kb // sp)
+        if tiles * sp > sms or per < 2 or (sp - 1) * per >= kb:
+            continue
+        split = sp
+    return tinym_b200.check_plan(1, n, k, tinym_b200.make_plan(
+        tinym_b200.KERNEL_SIMT_M1, split, stages, 0, cwarps, 128))
 
 
 def run_sweep(args, device):
@@ -540,8 +570,9 @@ def main():
     ap.add_argument("--no-fused-gather", action="store_true",
                     help="N > 1: skip the fused all-gather comparison")
     ap.add_argument("--plan", default=None,
-                    help="explicit TC plan 'split,stages,block_k,tile_m' instead of the "
-                         "dispatch table (re-measures one point of a plan sweep)")
+                    help="explicit TC plan 'split,stages,block_k,tile_m', or CUDA-core M=1 "
+                         "plan 'simt:split,stages,consumer_warps', instead of the dispatch "
+                         "table (re-measures one point of a plan sweep)")
     ap.add_argument("--scaling", choices=["weak", "strong"], default="strong",
                     help="N > 1: strong = the workload's N split over the ranks (value; "
                          "the fixed problem's N-sharded speed-up); weak = every rank owns a "
@@ -596,7 +627,12 @@ def main():
     sm_count = torch.cuda.get_device_properties(device).multi_processor_count
     plan = tinym_b200.select_plan(m, n_local, k, sm_count)
     explicit = None
-    if args.plan:
+    if args.plan and args.plan.startswith("simt:"):
+        sp, st, cw = (int(v) for v in args.plan[5:].split(","))
+        explicit = tinym_b200.check_plan(m, n_local, k, tinym_b200.make_plan(
+            tinym_b200.KERNEL_SIMT_M1, sp, st, 0, cw, 128))
+        plan = explicit
+    elif args.plan:
         sp, st, bk, tm = (int(v) for v in args.plan.split(","))
         explicit = tinym_b200.check_plan(m, n_local, k, tinym_b200.make_plan(
             tinym_b200.KERNEL_TC, sp, st, 8 if m <= 8 else 16, block_k=bk, tile_m=tm))

@@ -261,8 +261,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t pol_w = 0, pol_x = 0;
     // One stage = expect_tx(W + X bytes), then the W box and the X box on the
     // stage's full barrier (issue_w posts the expect_tx).
-    auto issue_w = [&](int i) {
-        const int s = i % stages;
+    // Stage i of this CTA's K range goes to ring slot s (= i mod stages; the
+    // loops below keep s and the slot's phase parity in running counters,
+    // since a runtime division per stage measurably slows the issue loops).
+    auto issue_w = [&](int i, int s) {
         const int chunk = (kb0 + i) * CHUNKS;  // first 128-byte K chunk of the stage
         mbar_expect_tx(full_bar(s), kStageTx);
         if (p.w_packed_kc) {
@@ -276,17 +278,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tma_load_3d(w_ring + s * kWStage, &tm_w, full_bar(s), 0, tile * TILE_M, chunk, pol_w);
         }
     };
-    auto issue_x = [&](int i) {
-        const int s = i % stages;
+    auto issue_x = [&](int i, int s) {
         const int chunk = (kb0 + i) * CHUNKS;
         if constexpr (CHUNKS == 1)
             tma_load_2d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), chunk * kBlockK, 0, pol_x);
         else
             tma_load_3d(x_ring + s * kXStageBytes, &tm_x, full_bar(s), 0, 0, chunk, pol_x);
     };
-    auto issue = [&](int i) {
-        issue_w(i);
-        issue_x(i);
+    auto issue = [&](int i, int s) {
+        issue_w(i, s);
+        issue_x(i, s);
     };
     if (threadIdx.x == 0) {
         TINYM_TRACE(0);
@@ -310,13 +311,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // kFlagEarlyW, which that kernel does not write.
         const int first = min(stages, n_issue);
         if (p.flags & kFlagEarlyW) {
-            for (int i = 0; i < first; ++i) issue_w(i);
+            for (int i = 0; i < first; ++i) issue_w(i, i);
             grid_dependency_wait();
-            for (; issued < first; ++issued) issue_x(issued);
+            for (; issued < first; ++issued) issue_x(issued, issued);
         } else {
             grid_dependency_wait();
             for (; issued < first; ++issued) {
-                issue(issued);
+                issue(issued, issued);
                 if (issued == 0) TINYM_TRACE(11);
             }
         }
@@ -354,11 +355,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer (refills the ring as slots free up)
+            // issued == min(stages, n_issue) here: slot 0 comes round again with
+            // the parity of its first use (0).
+            int s = 0;
+            uint32_t ph = 0u;
             for (; issued < n_issue; ++issued) {
-                const int s = issued % stages;
-                if (!mbar_wait(empty_bar(s), ((issued / stages) - 1) & 1, guard, kErrProducerWait))
-                    break;
-                issue(issued);
+                if (!mbar_wait(empty_bar(s), ph, guard, kErrProducerWait)) break;
+                issue(issued, s);
+                if (++s == stages) {
+                    s = 0;
+                    ph ^= 1u;
+                }
             }
             if (*abort_flag) {
                 // Drain the copies still in flight before shared memory is released.
@@ -375,10 +382,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t tmem_u = __shfl_sync(0xFFFFFFFFu, tmem_d, 0);
         const uint64_t da0 = sw128_kmajor_desc(w_ring);
         const uint64_t db0 = sw128_kmajor_desc(x_ring);
+        int s = 0;
+        uint32_t ph = 0u;
         for (int i = 0; i < nkb; ++i) {
-            const int s = i % stages;
             bool ok = true;
-            if (lane == 0) ok = mbar_wait(full_bar(s), (i / stages) & 1, guard, kErrMmaWait);
+            if (lane == 0) ok = mbar_wait(full_bar(s), ph, guard, kErrMmaWait);
             if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) break;
             if (lane == 0 && i == 0) TINYM_TRACE(3);
             if (lane == 0 && i == nkb - 1) TINYM_TRACE(4);
@@ -399,6 +407,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 umma_commit(empty_bar(s));  // frees the slot once these MMAs retire
             }
             __syncwarp();
+            if (++s == stages) {
+                s = 0;
+                ph ^= 1u;
+            }
         }
         if (lane == 0) {
             umma_commit(acc_bar);  // accumulator complete (or all issued MMAs retired)
@@ -606,8 +618,7 @@ __global__ void __launch_bounds__(32 * (CWARPS + 1), 1)
 
     int issued = 0;
     uint64_t pol_w = 0, pol_x = 0;
-    auto issue = [&](int i) {
-        const int s = i % stages;
+    auto issue = [&](int i, int s) {  // stage i into ring slot s (= i mod stages)
         const int kc = (kb0 + i) * kBlockK;
         mbar_expect_tx(full_bar(s), kStageTx);
         tma_load_2d(w_ring + s * kWStageBytes, &tm_w, full_bar(s), kc, tile * kTileRows, pol_w);
@@ -626,7 +637,7 @@ __global__ void __launch_bounds__(32 * (CWARPS + 1), 1)
         pol_w = l2_policy_w();
         pol_x = l2_policy_evict_last();
         grid_dependency_wait();
-        for (; issued < min(stages, n_issue); ++issued) issue(issued);  // first ring-full
+        for (; issued < min(stages, n_issue); ++issued) issue(issued, issued);  // first ring-full
         grid_launch_dependents();
     }
     __syncthreads();
@@ -642,11 +653,15 @@ __global__ void __launch_bounds__(32 * (CWARPS + 1), 1)
 
     if (warp == 0) {
         if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0u;
             for (; issued < n_issue; ++issued) {
-                const int s = issued % stages;
-                if (!mbar_wait(empty_bar(s), ((issued / stages) - 1) & 1, guard, kErrProducerWait))
-                    break;
-                issue(issued);
+                if (!mbar_wait(empty_bar(s), ph, guard, kErrProducerWait)) break;
+                issue(issued, s);
+                if (++s == stages) {
+                    s = 0;
+                    ph ^= 1u;
+                }
             }
             if (*abort_flag) {
                 for (int j = max(0, issued - stages); j < issued; ++j)
@@ -655,9 +670,10 @@ __global__ void __launch_bounds__(32 * (CWARPS + 1), 1)
         }
     } else {
         bool ok = true;
+        int s = 0;
+        uint32_t ph = 0u;
         for (int i = 0; i < nkb; ++i) {
-            const int s = i % stages;
-            if (!mbar_wait(full_bar(s), (i / stages) & 1, guard, kErrConsumerWait)) {
+            if (!mbar_wait(full_bar(s), ph, guard, kErrConsumerWait)) {
                 ok = false;
                 break;
             }
@@ -697,6 +713,10 @@ __global__ void __launch_bounds__(32 * (CWARPS + 1), 1)
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(empty_bar(s));
+            if (++s == stages) {
+                s = 0;
+                ph ^= 1u;
+            }
         }
         if (ok && !*abort_flag) {
 #pragma unroll

@@ -100,3 +100,41 @@ def test_noalloc_stream_ordered_reuse(cuda_device, oracle):
         y_ws, _ = tinym_b200.gemm_quant_act(x, w, w_scale)
         assert torch.equal(o, y_ws)
     assert tinym_b200.device_status() == 0
+
+
+@pytest.mark.gpu
+def test_noalloc_interleaved_with_early_weight_gemms(cuda_device, oracle):
+    """The static workspace stays consistent when no-allocation calls are
+    interleaved on one stream with plain GEMMs launched under programmatic
+    dependent launch with TINYM_FLAG_STATIC_W (the kernels that start
+    streaming before the previous kernel completes): the quantise prologue
+    is an ordinarily ordered launch, so it never overwrites the workspace
+    while an earlier GEMM still reads it."""
+    import torch
+
+    import tinym_b200
+
+    k, n = 2048, 640
+    _, wq, _, sw, _ = oracle.make_case(1, k, n, seed=6, dist="normal")
+    w = torch.from_numpy(wq).to(cuda_device).view(torch.float8_e4m3fn)
+    w_scale = torch.from_numpy(sw.astype(np.float32)).to(cuda_device)
+    xs = [torch.randn(m, k, device=cuda_device).to(torch.bfloat16) * s
+          for m, s in ((9, 1.0), (16, 50.0), (2, 1e-2))]
+    xq, _, _, _, alpha = oracle.make_case(9, k, 1, seed=7, dist="normal")
+    x8 = torch.from_numpy(xq).to(cuda_device).view(torch.float8_e4m3fn)
+    a8 = torch.from_numpy(alpha).to(cuda_device)
+    outs = [torch.empty((x.shape[0], n), dtype=torch.bfloat16, device=cuda_device) for x in xs]
+    plain = [torch.empty((9, n), dtype=torch.bfloat16, device=cuda_device) for _ in xs]
+    for _ in range(2):
+        for x, o, yp in zip(xs, outs, plain):
+            _noalloc(x, w, w_scale, o)
+            tinym_b200.gemm(x8, w, a8, out=yp, static_w=True)
+    torch.cuda.synchronize()
+    # the same plan as the static-W launches, without the flag: identical bits
+    sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
+    y_plain = tinym_b200.gemm(x8, w, a8, plan=tinym_b200.select_plan(9, n, k, sms, static_w=True))
+    for x, o, yp in zip(xs, outs, plain):
+        y_ws, _ = tinym_b200.gemm_quant_act(x, w, w_scale)
+        assert torch.equal(o, y_ws)
+        assert torch.equal(yp, y_plain)
+    assert tinym_b200.device_status() == 0

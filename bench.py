@@ -270,20 +270,39 @@ def per_launch_latency(fn, sets, n, flush=None, seed=0):
     return [s.elapsed_time(e) for s, e in zip(starts, ends)]
 
 
+MIN_REPLAY_LAUNCHES = 40  # a replay shorter than this pays visible per-replay overhead
+
+
+def replay_sizes(steps, target_chunks=5):
+    """Launches per CUDA-graph replay for `steps` timed steps (they sum to
+    `steps`): about `target_chunks` equal replays of at least
+    MIN_REPLAY_LAUNCHES launches, one replay below twice that."""
+    if steps < 1:
+        raise ValueError("steps must be positive")
+    r = max(min(steps, MIN_REPLAY_LAUNCHES), steps // max(1, target_chunks))
+    if steps < 2 * MIN_REPLAY_LAUNCHES:
+        r = steps
+    return [r] * (steps // r) + ([steps % r] if steps % r else [])
+
+
 def graph_chunks(fn, sets, steps, warmup, target_chunks=5):
     """Time exactly `steps` back-to-back launches as a few CUDA-graph replays.
 
-    The steps are cut into chunks of R = max(1, steps // target_chunks)
-    launches (the last one may be shorter), each chunk a graph over the
-    rotating `sets`.  All replays are queued behind a spin spacer, so they
-    run back to back on the device, with an event between consecutive
-    replays.  Returns (total_ms, [(launches, ms) per chunk]); the median of
-    the per-chunk ms per launch is robust against a single slow replay.
+    The steps are cut into chunks of R launches (the last one may be
+    shorter), each chunk a graph over the rotating `sets`: about
+    `target_chunks` chunks, but never fewer than MIN_REPLAY_LAUNCHES
+    launches per chunk (fewer steps than twice that run as one replay), so
+    that neither the start of a replay nor the ~1-2 us step of the event
+    timestamps weighs on the per-launch time.  All replays are queued
+    behind a spin spacer, so they run back to back on the device, with an
+    event between consecutive replays.  Returns (total_ms, [(launches, ms)
+    per chunk]); the median of the per-chunk ms per launch is robust
+    against a single slow replay.
     """
     import torch
 
-    r = max(1, steps // max(1, target_chunks))
-    sizes = [r] * (steps // r) + ([steps % r] if steps % r else [])
+    sizes = replay_sizes(steps, target_chunks)
+    r = sizes[0]
     graphs = {}
     stream = torch.cuda.Stream()
     stream.wait_stream(torch.cuda.current_stream())

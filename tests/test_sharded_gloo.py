@@ -171,3 +171,19 @@ def test_bench_rank_slabs(world):
         bench.rank_slab(5120, 3, "strong")
     with pytest.raises(ValueError):
         bench.rank_slab(5120, world, "diagonal")
+
+
+def test_bench_replay_sizes():
+    """The bench times exactly K steps as CUDA-graph replays of at least 40
+    launches (one replay below 80 steps), about five replays otherwise."""
+    import bench
+
+    for steps in (1, 20, 79, 80, 100, 200, 1000, 12345):
+        sizes = bench.replay_sizes(steps)
+        assert sum(sizes) == steps
+        if steps < 80:
+            assert sizes == [steps]
+        else:
+            assert min(sizes[:-1] or sizes) >= 40 and len(sizes) <= 6
+    with pytest.raises(ValueError):
+        bench.replay_sizes(0)

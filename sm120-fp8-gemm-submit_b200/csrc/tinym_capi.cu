@@ -688,6 +688,7 @@ static int gemm_prepare(const void* x, const void* w, void* y, int64_t ldy, int6
     prm.flags = flags & 0xFFFFu;  // the kernel's kFlag* bits only
     prm.timeout_ns = timeout_ns;
     prm.w_packed_kc = w_packed ? static_cast<int32_t>(tinym::packed_chunks(k)) : 0;
+    prm.rpo = tinym::tc_rows_per_owner(p.tile_m, p.split_k);
     if ((st = pending_word(di, may_allocate, &prm.err_host)) != TINYM_OK) return st;
     if (gd) {
         // CTA (0,0) waits for the other ranks: the whole grid must be resident

@@ -44,14 +44,19 @@ namespace tinym {
 __device__ uint32_t g_err_word;
 
 // Timeline trace points.  They compile to nothing unless a diagnostic build
-// defines TINYM_TRACE_POINTS, in which case the %globaltimer value of each
-// event is recorded per CTA in g_trace (latency analysis only; the shipped
-// library never defines it).
+// defines TINYM_TRACE_POINTS, in which case the SM cycle counter of each
+// event is recorded per CTA in g_trace, and %globaltimer at the CTA's first
+// and last event in g_trace_ns (to align CTAs and convert cycles; the
+// timer itself ticks in coarse steps).  Latency analysis only; the shipped
+// library never defines it.
 #ifdef TINYM_TRACE_POINTS
-__device__ uint64_t g_trace[8192][16];
-#define TINYM_TRACE(id) (g_trace[blockIdx.y * gridDim.x + blockIdx.x][(id)] = globaltimer_ns())
+__device__ uint64_t g_trace[8192][24];
+__device__ uint64_t g_trace_ns[8192][2];
+#define TINYM_TRACE(id) (g_trace[blockIdx.y * gridDim.x + blockIdx.x][(id)] = clock64())
+#define TINYM_TRACE_NS(slot) (g_trace_ns[blockIdx.y * gridDim.x + blockIdx.x][(slot)] = globaltimer_ns())
 #else
 #define TINYM_TRACE(id) ((void)0)
+#define TINYM_TRACE_NS(slot) ((void)0)
 #endif
 
 enum : uint32_t {
@@ -82,6 +87,7 @@ struct TinymParams {
     uint32_t flags;        // kFlag* bits (0 in normal operation)
     uint64_t timeout_ns;   // limit of every mbarrier wait
     int32_t w_packed_kc;   // 0: W row-major [N, K]; else W packed, this many K chunks per tile
+    int32_t rpo;           // TC split-K: tile rows each cluster rank owns (tc_rows_per_owner)
     // Fused all-gather of the N-sharded wrapper (n_peers > 0): the BF16 rows
     // go to every rank's full Y (peer_y[r] = rank r's Y + this rank's first
     // column, row stride ldy) instead of y, each CTA then adds the number of
@@ -142,7 +148,7 @@ __host__ __device__ inline SmemLayout smem_layout(int stages, int w_stage_bytes,
     L.red_off = (L.red_off + 15u) & ~15u;
     const uint32_t red_bytes = static_cast<uint32_t>((split - 1) * red_rank_bytes);
     L.bar_off = (L.red_off + red_bytes + 7u) & ~7u;
-    L.misc_off = L.bar_off + static_cast<uint32_t>(2 * stages + 2) * 8u;
+    L.misc_off = L.bar_off + static_cast<uint32_t>(2 * stages + 3) * 8u;
     // +1024: the dynamic window is re-aligned to 1024 bytes in the kernel.
     L.bytes = L.misc_off + 16u + 1024u;
     return L;
@@ -216,7 +222,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
-    const int red_rank_bytes = tc_red_rank_bytes(MMA_N, TILE_M, p.split);
+    // Rows of the tile each cluster rank sums and stores (host-computed
+    // tc_rows_per_owner: no division on the device).
+    const int rpo = p.rpo;
+    const int red_rank_bytes = rpo * kRedStride * 4;  // tc_red_rank_bytes
     const SmemLayout L = smem_layout(p.stages, kWStage, kXStageBytes, p.split, red_rank_bytes);
     const uint32_t s_base = smem_u32(smem);
     const uint32_t w_ring = s_base + L.w_off;
@@ -227,23 +236,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     auto empty_bar = [&](int s) { return bars + 8u * (stages + s); };
     const uint32_t acc_bar = bars + 8u * (2 * stages);
     const uint32_t red_bar = bars + 8u * (2 * stages + 1);
+    // One arrive per epilogue warp once its accumulator reads are complete:
+    // the MMA warp then frees TMEM while the epilogue is still running.
+    const uint32_t tmem_bar = bars + 8u * (2 * stages + 2);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.misc_off);
     volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L.misc_off + 4);
-    // Partial sums from the other ranks land in their own region; after the
-    // mainloop the X ring stages the BF16 output rows.
+    // Partial sums from the other ranks land in their own region.
     float* red = reinterpret_cast<float*>(smem + L.red_off);
-    __nv_bfloat16* ystage = reinterpret_cast<__nv_bfloat16*>(smem + L.x_off);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int split_idx = blockIdx.x;
     const int tile = blockIdx.y;
     const bool clustered = p.split > 1;
-    // Rows of the tile this CTA sums and stores, and the partial-sum columns
-    // that carry data (X rows m < M, in groups of four).
-    const int rpo = tc_rows_per_owner(TILE_M, p.split);
+    // Rows of the tile this CTA sums and stores (tc_rows_owned), and the
+    // partial-sum columns that carry data (X rows m < M, in groups of four).
     const int own_lo = split_idx * rpo;
-    const int own_cnt = tc_rows_owned(TILE_M, p.split, split_idx);
+    const int own_cnt = max(0, min(rpo, TILE_M - own_lo));
     const int red_cols = (p.m + 3) & ~3;
     const int kb0 = split_idx * p.kb_per_split;
     const int kb1 = min(kb0 + p.kb_per_split, p.kb_total);
@@ -290,16 +299,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         issue_x(i, s);
     };
     if (threadIdx.x == 0) {
+        TINYM_TRACE_NS(0);
         TINYM_TRACE(0);
         tma_prefetch_desc(&tm_w);
         tma_prefetch_desc(&tm_x);
-        for (int s = 0; s < stages; ++s) {
-            mbar_init(full_bar(s), 1);
-            mbar_init(empty_bar(s), 1);
-        }
-        mbar_init(acc_bar, 1);
-        mbar_init(red_bar, 1);
-        *abort_flag = 0u;
+        // The first ring-full of loads goes out before anything else: only
+        // the full barriers are initialised (and published to the async
+        // proxy) ahead of it; the other barriers follow while it is in flight.
+        for (int s = 0; s < stages; ++s) mbar_init(full_bar(s), 1);
         fence_mbar_init();
         fence_proxy_async_smem();
         TINYM_TRACE(10);
@@ -324,6 +331,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // Let the next kernel in the stream start its own prologue on SMs
         // as they free up (it still waits for this grid to complete).
         grid_launch_dependents();
+        for (int s = 0; s < stages; ++s) mbar_init(empty_bar(s), 1);
+        mbar_init(acc_bar, 1);
+        mbar_init(red_bar, 1);
+        mbar_init(tmem_bar, 4);
+        *abort_flag = 0u;
+        fence_mbar_init();
         TINYM_TRACE(1);
         // This CTA's rows arrive from every other rank of the cluster
         // (st.async, completing their bytes on red_bar).
@@ -415,7 +428,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0) {
             umma_commit(acc_bar);  // accumulator complete (or all issued MMAs retired)
             if (*abort_flag) mbar_drain(acc_bar, 0, guard, kErrDrain);
+            // Free TMEM as soon as every epilogue warp has read it (each
+            // arrives even without an accumulator), off the output path.
+            mbar_drain(tmem_bar, 0, guard, kErrDrain);
         }
+        __syncwarp();
+        tc_fence_after_sync();
+        tmem_dealloc(tmem_d, kTmemCols);
+        if (threadIdx.x == 32) TINYM_TRACE(9);
     } else {
         // ---------------- epilogue warps 2..5: TMEM lanes 32*(warp%4) ..
         grid_dependency_wait();  // alpha may be written by the previous kernel
@@ -425,8 +445,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(alpha) : "l"(p.alpha_ptr) : "memory");
         else
             alpha = p.alpha;
+        // The cluster barrier (every CTA of the cluster resident, barriers
+        // initialised) completes long before the first remote store; waiting
+        // here keeps the wait off the output path.
+        if (clustered) cluster_wait_acquire();
         // tcgen05.ld is .sync.aligned: the whole warp takes the same branch.
         const bool ready = mbar_wait(acc_bar, 0, guard, kErrEpilogueWait) && !*abort_flag;
+        if (threadIdx.x == 64) TINYM_TRACE(16);
         if (__all_sync(0xFFFFFFFFu, ready)) {
             tc_fence_after_sync();
             const uint32_t taddr = tmem_d + (static_cast<uint32_t>((warp & 3) * 32) << 16);
@@ -438,8 +463,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             have_acc = true;
             if (threadIdx.x == 64) TINYM_TRACE(5);
         }
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tmem_bar);
     }
-    __syncwarp();
+    // Warps 0 and 1 are done (the producer and the MMA warp exit here; the
+    // MMA warp has freed TMEM).  No CTA-wide barrier follows: the epilogue
+    // warps finish the reduction and the stores on their own.
+    if (warp < 2) return;
 
     // ---------------- split-K reduce-scatter through distributed shared memory
     // Epilogue thread (warp w, lane t) holds TMEM lane 32*(w%4)+t, which is
@@ -449,7 +480,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const bool row_ok = epi && lane < kRowsPerWarp;
     const bool row_mine = row_ok && row >= own_lo && row < own_lo + own_cnt;
     if (clustered) {
-        cluster_wait_acquire();
         if (threadIdx.x == 64) TINYM_TRACE(6);
         if (row_ok && !row_mine) {
             // Push this row's partial sums to the owner's block for this
@@ -510,72 +540,53 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
     }
 
-    // ---------------- output: this CTA's rows, staged in shared memory as
-    // BF16, then written with 16-byte stores (8 consecutive N per store).
-    if (epi) {
-        if (have_acc && row_mine) {
-#pragma unroll
-            for (int m = 0; m < MMA_N; ++m)
-                ystage[m * TILE_M + row] = __float2bfloat16_rn(acc[m] * alpha);
-        }
-        if (threadIdx.x == 64) TINYM_TRACE(15);
-        epilogue_bar_sync();  // the 4 epilogue warps only
-        if (threadIdx.x == 64) TINYM_TRACE(13);
-        if (!*abort_flag) {
-            const int n0 = tile * TILE_M;
-            const int vecs = own_cnt / 8;  // 16-byte vectors per output row
+    // ---------------- output: each owner thread converts its row's M values
+    // and stores them straight from registers (for each m, the lanes of a
+    // warp write consecutive N: one coalesced segment per warp and m).
+    if (threadIdx.x == 64) TINYM_TRACE(15);
+    if (have_acc && row_mine && !*abort_flag) {
+        const int n = tile * TILE_M + row;
+        if (n < p.n) {
             // Destinations: y, or this rank's column block of every rank's
             // full Y (peer stores over NVLink for r != rank).
             const int ndst = p.n_peers > 0 ? p.n_peers : 1;
+#pragma unroll 1
             for (int d = 0; d < ndst; ++d) {
-                __nv_bfloat16* base = p.n_peers > 0 ? p.peer_y[d] : p.y;
-                const bool vec = ((reinterpret_cast<uintptr_t>(base) & 15u) == 0) && (p.ldy % 8 == 0);
-                for (int c = threadIdx.x - 64; c < p.m * vecs; c += 128) {
-                    const int m = c / vecs;
-                    const int j = own_lo + (c % vecs) * 8;
-                    const __nv_bfloat16* src = ystage + m * TILE_M + j;
-                    __nv_bfloat16* dst = base + static_cast<size_t>(m) * p.ldy + n0 + j;
-                    if (vec && n0 + j + 8 <= p.n) {
-                        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
-                    } else {
-                        for (int e = 0; e < 8 && n0 + j + e < p.n; ++e) dst[e] = src[e];
-                    }
-                }
+                __nv_bfloat16* dst = (p.n_peers > 0 ? p.peer_y[d] : p.y) + n;
+#pragma unroll
+                for (int m = 0; m < MMA_N; ++m)
+                    if (m < p.m) dst[static_cast<size_t>(m) * p.ldy] = __float2bfloat16_rn(acc[m] * alpha);
             }
-            if (p.n_peers > 0) {
-                // Every store of this CTA (the named barrier orders them
-                // before thread 64), then one release per rank at system
-                // scope: its counter grows by the elements this CTA wrote.
-                epilogue_bar_sync();
-                if (threadIdx.x == 64) {
-                    const int cols = max(0, min(own_cnt, p.n - (n0 + own_lo)));
-                    const unsigned long long cnt = static_cast<unsigned long long>(p.m) * cols;
-                    fence_acq_rel_sys();
-                    for (int d = 0; d < p.n_peers; ++d) red_relaxed_sys_add_u64(p.peer_flag[d], cnt);
-                    if (blockIdx.x == 0 && blockIdx.y == 0) {
-                        // Bounded wait for every rank's rows of this call.
-                        const uint64_t t0 = globaltimer_ns();
-                        while (ld_acquire_sys_u64(p.peer_flag[p.rank]) < p.gather_target) {
-                            if (globaltimer_ns() - t0 > p.timeout_ns) {
-                                report_timeout(&g_err_word, p.err_host, kErrPeerWait);
-                                break;
-                            }
-                            __nanosleep(32);
-                        }
+        }
+    }
+    if (threadIdx.x == 64) TINYM_TRACE(8);
+    if (p.n_peers > 0) {
+        // Every store of this CTA (the named barrier orders them before
+        // thread 64), then one release per rank at system scope: its
+        // counter grows by the elements this CTA wrote.
+        epilogue_bar_sync();
+        if (threadIdx.x == 64 && !*abort_flag) {
+            const int n0 = tile * TILE_M;
+            const int cols = max(0, min(own_cnt, p.n - (n0 + own_lo)));
+            const unsigned long long cnt = static_cast<unsigned long long>(p.m) * cols;
+            fence_acq_rel_sys();
+            for (int d = 0; d < p.n_peers; ++d) red_relaxed_sys_add_u64(p.peer_flag[d], cnt);
+            if (blockIdx.x == 0 && blockIdx.y == 0) {
+                // Bounded wait for every rank's rows of this call.
+                const uint64_t t0 = globaltimer_ns();
+                while (ld_acquire_sys_u64(p.peer_flag[p.rank]) < p.gather_target) {
+                    if (globaltimer_ns() - t0 > p.timeout_ns) {
+                        report_timeout(&g_err_word, p.err_host, kErrPeerWait);
+                        break;
                     }
+                    __nanosleep(32);
                 }
             }
         }
     }
-
-    // ---------------- teardown
-    if (threadIdx.x == 64) TINYM_TRACE(8);
-    tc_fence_before_sync();
-    __syncthreads();
-    if (warp == 1) {
-        tc_fence_after_sync();
-        tmem_dealloc(tmem_d, kTmemCols);
-        if (threadIdx.x == 32) TINYM_TRACE(9);
+    if (threadIdx.x == 64) {
+        TINYM_TRACE(17);
+        TINYM_TRACE_NS(1);
     }
 }
 

@@ -33,12 +33,12 @@
 namespace {
 
 using tinym::kBlockK;
+using tinym::kMaxSplit;  // portable cluster size
 using tinym::kTcThreads;
 using tinym::kTileRows;
 using tinym::TinymParams;
 
 constexpr int kMaxDevices = 64;
-constexpr int kMaxSplit = 8;       // portable cluster size
 constexpr int kMaxStages = 32;
 constexpr int kSmemLimit = 232448; // 227 KiB opt-in per CTA on sm_100
 constexpr uint64_t kDefaultTimeoutNs = 1000000000ull;  // 1 s per wait

@@ -74,6 +74,7 @@ constexpr int kBlockK = 128;     // K bytes of one chunk (= one 128B swizzle row
 constexpr int kWStageBytes = kTileRows * kBlockK;  // one W chunk: 16 KiB
 constexpr int kTcThreads = 192;  // warp0 TMA, warp1 MMA, warps2-5 epilogue
 constexpr int kTmemCols = 32;    // minimum allocation; MMA_N <= 16 columns used
+constexpr int kMaxSplit = 8;     // CTAs per cluster (K split), portable cluster size
 
 struct TinymParams {
     __nv_bfloat16* y;
@@ -508,25 +509,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const bool got = mbar_drain(red_bar, 0, guard, kErrReduceWait);
             if (threadIdx.x == 64) TINYM_TRACE(7);
             if (got && have_acc) {
+                // Ranks in order (rank 0 first); the loop is unrolled so that
+                // the compiler can issue every rank's loads before the adds.
+                const float* mine = red + (row - own_lo) * kRedStride;
                 float sum[MMA_N];
 #pragma unroll
                 for (int c = 0; c < MMA_N; ++c) sum[c] = 0.f;
-                for (int r = 0; r < p.split; ++r) {
-                    if (r == split_idx) {
 #pragma unroll
-                        for (int c = 0; c < MMA_N; ++c) sum[c] += acc[c];
-                    } else {
-                        const int slot = r < split_idx ? r : r - 1;
-                        const float4* part = reinterpret_cast<const float4*>(
-                            red + slot * (red_rank_bytes / 4) + (row - own_lo) * kRedStride);
+                for (int r = 0; r < kMaxSplit; ++r) {
+                    if (r < p.split) {
+                        if (r == split_idx) {
 #pragma unroll
-                        for (int c = 0; c < MMA_N / 4; ++c) {
-                            if (4 * c < red_cols) {
-                                const float4 q = part[c];
-                                sum[4 * c + 0] += q.x;
-                                sum[4 * c + 1] += q.y;
-                                sum[4 * c + 2] += q.z;
-                                sum[4 * c + 3] += q.w;
+                            for (int c = 0; c < MMA_N; ++c) sum[c] += acc[c];
+                        } else {
+                            const float4* part = reinterpret_cast<const float4*>(
+                                mine + (r < split_idx ? r : r - 1) * (red_rank_bytes / 4));
+#pragma unroll
+                            for (int c = 0; c < MMA_N / 4; ++c) {
+                                if (4 * c < red_cols) {
+                                    const float4 q = part[c];
+                                    sum[4 * c + 0] += q.x;
+                                    sum[4 * c + 1] += q.y;
+                                    sum[4 * c + 2] += q.z;
+                                    sum[4 * c + 3] += q.w;
+                                }
                             }
                         }
                     }

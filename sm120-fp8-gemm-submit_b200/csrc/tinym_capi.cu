@@ -372,6 +372,8 @@ constexpr uint32_t kFlagQuantPrologue = 1u << 16;
 // stream W during its tail: measured 4-9 % more back-to-back throughput at
 // M = 9 on the official points.
 constexpr int kOverlapRingBytes = 64 * 1024;
+// W in flight per CTA for the 64-row full-K plans (fewer, longer-lived CTAs).
+constexpr int kFullKRingBytes = 160 * 1024;
 constexpr uint32_t kHalfSmSmem = (233472u - 2u * 1024u) / 2u;  // two CTAs' share of an SM
 
 // Ring depth for a TC plan: ring_bytes of W in flight, at most what fits
@@ -385,19 +387,25 @@ int tc_stages_for(const tinym_plan& p, int64_t kb_per_cta, int ring_bytes = kTar
 }
 
 // Heuristic part of the dispatch table, fitted to B200 measurements of the
-// official points (plan sweeps, per-CTA %globaltimer traces):
+// official points (plan sweeps, per-CTA cycle traces):
 //  * one CTA per SM with a deep ring (two CTAs per SM never won);
 //  * block_k = 256 -- one 32 KiB 3-D TMA box of W per stage -- whenever
-//    K % 128 == 0, else 128.  A CTA streams W at ~40 GB/s with 16 KiB
-//    boxes (a per-stage cost that neither ring depth nor a contiguous W
-//    layout removes), while 64 KiB stages make the tensor core's drain of
-//    the last stage (~0.5 us) and the start-up longer; 32 KiB x 4 stages
-//    measured best in the harness protocol at every official point;
-//  * 128-row W tiles (64-row tiles need no K split on N = 5120 / 8192 but
-//    stream only ~37 GB/s per CTA with 32 KiB boxes, which loses);
-//  * the largest K split (cluster size <= 8) that keeps tiles * split CTAs
-//    within one CTA per SM and gives every CTA >= 2 stages;
-//  * a ring of ~128 KiB of W (tc_stages_for).
+//    K % 128 == 0, else 128.  A CTA's TMA stream costs ~150 ns per box
+//    whatever its size up to 32 KiB (54 GB/s per CTA with 8 KiB boxes, 106
+//    with 16 KiB, ~150-190 with 32 KiB, measured with few CTAs), while
+//    64 KiB stages lengthen the tensor core's drain of the last stage and
+//    the start-up; 32 KiB x 4 stages measured best at every official point;
+//  * 128-row W tiles and the largest K split (cluster size <= 8) that keeps
+//    tiles * split CTAs within one CTA per SM and gives every CTA >= 2
+//    stages, with a ring of ~128 KiB of W (tc_stages_for);
+//  * except for M > 8 when that split is 3 or more and there are enough
+//    64-row tiles to keep about half of the SMs streaming (e.g. N = 5120):
+//    64-row tiles with full K, one 32 KiB box of 64 rows x 512 B per stage
+//    and a ~160 KiB ring, no reduction -- 0.25-0.3 us faster back to back
+//    at (9..16, 6144, 5120) and the same per single launch.  For M <= 8 the
+//    two are equal back to back and the split plan is ~0.2 us faster per
+//    single launch; at N = 8192 (split 2) the split plan wins single
+//    launches by ~0.3 us.
 // overlap = true: the TINYM_FLAG_STATIC_W variant (two CTAs per SM).
 tinym_plan heuristic_plan(int64_t m, int64_t n, int64_t k, int sm_count, bool overlap = false) {
     tinym_plan p{};
@@ -425,6 +433,19 @@ tinym_plan heuristic_plan(int64_t m, int64_t n, int64_t k, int sm_count, bool ov
         p.split_k = s;
     }
     p.stages = tc_stages_for(p, (kb + p.split_k - 1) / p.split_k, ring);
+    if (!overlap && m > 8 && p.split_k >= 3 && k % kBlockK == 0) {
+        tinym_plan q = p;
+        q.tile_m = 64;
+        q.split_k = 1;
+        q.block_k = 4 * kBlockK;
+        const int64_t tiles64 = (n + q.tile_m - 1) / q.tile_m;
+        const int64_t kb64 = (k + q.block_k - 1) / q.block_k;
+        const int st = tc_stages_for(q, kb64, kFullKRingBytes);
+        if (tiles64 <= slots && 2 * tiles64 >= slots && kb64 >= 4 && st >= 4) {
+            q.stages = st;
+            p = q;
+        }
+    }
     return p;
 }
 

@@ -567,8 +567,7 @@ def run_sweep(args, device):
     for (k, n) in ((6144, 5120), (5120, 8192), (5120, 16384)):
         for m in range(1, 17):
             for d in dists:
-                p = measure_point(m, k, n, device, l2, peak, w_dist=d, lat_n=40, graph_steps=60,
-                                  seed=m * 1000 + n)
+                p = measure_point(m, k, n, device, l2, peak, w_dist=d, seed=m * 1000 + n)
                 print(json.dumps(p), flush=True)
 
 

@@ -670,8 +670,13 @@ static int gemm_prepare(const void* x, const void* w, void* y, int64_t ldy, int6
             int clusters = 0;
             if ((st = max_active_clusters(p, dev, di, &clusters)) != TINYM_OK) return st;
             if (clusters >= p.tiles_n) break;
-            --p.split_k;
+            // The next smaller split that leaves no CTA an empty K range
+            // (e.g. 20 K blocks: 7 -> 5, since a split of 6 leaves rank 5
+            // nothing).
             const int64_t kb = (k + p.block_k - 1) / p.block_k;
+            do {
+                --p.split_k;
+            } while (p.split_k > 1 && (p.split_k - 1) * ((kb + p.split_k - 1) / p.split_k) >= kb);
             const int s2 = p.kernel == TINYM_KERNEL_TC
                                ? tc_stages_for(p, (kb + p.split_k - 1) / p.split_k, ring)
                                : p.stages;

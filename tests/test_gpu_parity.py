@@ -140,6 +140,22 @@ def test_ragged_shapes(cuda_device, oracle, m, k, n):
     _check(oracle, out, xq, wq, alpha)
 
 
+@pytest.mark.parametrize("m,k,n", [(9, 5120, 2048), (1, 5120, 2048), (9, 5120, 4096),
+                                   (9, 6144, 640), (16, 5120, 1024)])
+def test_sharded_slab_shapes(cuda_device, oracle, m, k, n):
+    """The per-rank slabs of the N-sharded bench (16384 / 8 or / 4, 5120 / 8):
+    the dispatch's K split is large there, and when the device cannot hold
+    every cluster at once the launcher shrinks the split to the next value
+    that still gives every CTA of a cluster some K."""
+    import torch
+
+    xq, wq, sx, sw, alpha = oracle.make_case(m, k, n, seed=m * 7 + n, dist="normal")
+    x, w = _to_dev(xq, cuda_device), _to_dev(wq, cuda_device)
+    out = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=cuda_device)
+    _run(x, w, torch.from_numpy(alpha).to(cuda_device), out=out)
+    _check(oracle, out, xq, wq, alpha)
+
+
 def _valid(tinym_b200, m, k, n, plan):
     try:
         tinym_b200.check_plan(m, n, k, plan)

@@ -366,6 +366,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     bool have_acc = false;
     float alpha = 0.f;
 
+    // Epilogue thread (warp w, lane t) holds TMEM lane 32*(w%4)+t, which is
+    // tile row (w%4)*kRowsPerWarp + t for t < kRowsPerWarp.
+    const int row = (warp & 3) * kRowsPerWarp + lane;
+    const bool epi = warp >= 2;
+    const bool row_ok = epi && lane < kRowsPerWarp;
+    const bool row_mine = row_ok && row >= own_lo && row < own_lo + own_cnt;
+    // Split-K senders: the owner's receive slot and barrier in cluster
+    // addresses, computed while the mainloop runs (off the output path).
+    uint32_t send_dst = 0u, send_bar = 0u;
+
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer (refills the ring as slots free up)
@@ -450,6 +460,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // initialised) completes long before the first remote store; waiting
         // here keeps the wait off the output path.
         if (clustered) cluster_wait_acquire();
+        if (clustered && row_ok && !row_mine) {
+            const int owner = row / rpo;
+            const int slot = split_idx < owner ? split_idx : split_idx - 1;
+            send_dst = dsmem_map(smem_u32(red), static_cast<uint32_t>(owner)) +
+                       static_cast<uint32_t>(slot * red_rank_bytes +
+                                             (row - owner * rpo) * kRedStride * 4);
+            send_bar = dsmem_map(red_bar, static_cast<uint32_t>(owner));
+        }
         // tcgen05.ld is .sync.aligned: the whole warp takes the same branch.
         const bool ready = mbar_wait(acc_bar, 0, guard, kErrEpilogueWait) && !*abort_flag;
         if (threadIdx.x == 64) TINYM_TRACE(16);
@@ -474,31 +492,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (warp < 2) return;
 
     // ---------------- split-K reduce-scatter through distributed shared memory
-    // Epilogue thread (warp w, lane t) holds TMEM lane 32*(w%4)+t, which is
-    // tile row (w%4)*kRowsPerWarp + t for t < kRowsPerWarp.
-    const int row = (warp & 3) * kRowsPerWarp + lane;
-    const bool epi = warp >= 2;
-    const bool row_ok = epi && lane < kRowsPerWarp;
-    const bool row_mine = row_ok && row >= own_lo && row < own_lo + own_cnt;
     if (clustered) {
         if (threadIdx.x == 64) TINYM_TRACE(6);
         if (row_ok && !row_mine) {
             // Push this row's partial sums to the owner's block for this
             // rank.  Every such thread always sends (zeros if it has no
             // accumulator) so the owner's wait ends.
-            const int owner = row / rpo;
-            const int slot = split_idx < owner ? split_idx : split_idx - 1;
-            const uint32_t dst = dsmem_map(smem_u32(red), static_cast<uint32_t>(owner)) +
-                                 static_cast<uint32_t>(slot * red_rank_bytes +
-                                                       (row - owner * rpo) * kRedStride * 4);
-            const uint32_t rbar = dsmem_map(red_bar, static_cast<uint32_t>(owner));
 #pragma unroll
             for (int c = 0; c < MMA_N; c += 4) {
                 if (c < red_cols) {
                     float v[4];
 #pragma unroll
                     for (int j = 0; j < 4; ++j) v[j] = have_acc ? acc[c + j] : 0.f;
-                    st_async_v4(dst + 16u * (c / 4), v, rbar);
+                    st_async_v4(send_dst + 16u * (c / 4), v, send_bar);
                 }
             }
             if (threadIdx.x == 160) TINYM_TRACE(14);

@@ -482,22 +482,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             have_acc = true;
             if (threadIdx.x == 64) TINYM_TRACE(5);
         }
-        tc_fence_before_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(tmem_bar);
-    }
-    // Warps 0 and 1 are done (the producer and the MMA warp exit here; the
-    // MMA warp has freed TMEM).  No CTA-wide barrier follows: the epilogue
-    // warps finish the reduction and the stores on their own.
-    if (warp < 2) return;
-
-    // ---------------- split-K reduce-scatter through distributed shared memory
-    if (clustered) {
-        if (threadIdx.x == 64) TINYM_TRACE(6);
-        if (row_ok && !row_mine) {
-            // Push this row's partial sums to the owner's block for this
-            // rank.  Every such thread always sends (zeros if it has no
-            // accumulator) so the owner's wait ends.
+        if (clustered && row_ok && !row_mine) {
+            // Split-K: push this row's partial sums to the owner's block for
+            // this rank straight away (TMEM is released just after).  Every
+            // such thread always sends (zeros if it has no accumulator) so
+            // the owner's wait ends.
 #pragma unroll
             for (int c = 0; c < MMA_N; c += 4) {
                 if (c < red_cols) {
@@ -508,7 +497,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
             if (threadIdx.x == 160) TINYM_TRACE(14);
-        } else if (row_mine) {
+        }
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tmem_bar);
+    }
+    // Warps 0 and 1 are done (the producer and the MMA warp exit here; the
+    // MMA warp has freed TMEM).  No CTA-wide barrier follows: the epilogue
+    // warps finish the reduction and the stores on their own.
+    if (warp < 2) return;
+
+    // ---------------- split-K reduce-scatter through distributed shared memory
+    // (the senders pushed their rows right after reading the accumulator)
+    if (clustered) {
+        if (threadIdx.x == 64) TINYM_TRACE(6);
+        if (row_mine) {
             // Owner: wait for the other ranks' partials of this row (bounded),
             // then add all ranks in K order (rank 0 first), so the result
             // does not depend on arrival order or on which rank owns the row.

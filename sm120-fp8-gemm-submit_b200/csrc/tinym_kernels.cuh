@@ -384,7 +384,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             int s = 0;
             uint32_t ph = 0u;
             for (; issued < n_issue; ++issued) {
-                if (!mbar_wait(empty_bar(s), ph, guard, kErrProducerWait)) break;
+                if (!mbar_wait_inline(empty_bar(s), ph, guard, kErrProducerWait, true)) break;
                 issue(issued, s);
                 if (++s == stages) {
                     s = 0;
@@ -410,7 +410,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         uint32_t ph = 0u;
         for (int i = 0; i < nkb; ++i) {
             bool ok = true;
-            if (lane == 0) ok = mbar_wait(full_bar(s), ph, guard, kErrMmaWait);
+            if (lane == 0) ok = mbar_wait_inline(full_bar(s), ph, guard, kErrMmaWait, true);
             if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) break;
             if (lane == 0 && i == 0) TINYM_TRACE(3);
             if (lane == 0 && i == nkb - 1) TINYM_TRACE(4);
@@ -469,7 +469,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             send_bar = dsmem_map(red_bar, static_cast<uint32_t>(owner));
         }
         // tcgen05.ld is .sync.aligned: the whole warp takes the same branch.
-        const bool ready = mbar_wait(acc_bar, 0, guard, kErrEpilogueWait) && !*abort_flag;
+        const bool ready =
+            mbar_wait_inline(acc_bar, 0, guard, kErrEpilogueWait, true) && !*abort_flag;
         if (threadIdx.x == 64) TINYM_TRACE(16);
         if (__all_sync(0xFFFFFFFFu, ready)) {
             tc_fence_after_sync();
@@ -515,7 +516,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             // Owner: wait for the other ranks' partials of this row (bounded),
             // then add all ranks in K order (rank 0 first), so the result
             // does not depend on arrival order or on which rank owns the row.
-            const bool got = mbar_drain(red_bar, 0, guard, kErrReduceWait);
+            const bool got = mbar_wait_inline(red_bar, 0, guard, kErrReduceWait, false);
             if (threadIdx.x == 64) TINYM_TRACE(7);
             if (got && have_acc) {
                 // Ranks in order (rank 0 first); the loop is unrolled so that

@@ -126,6 +126,26 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const W
     return mbar_wait_slow(bar, parity, g, code, true);
 }
 
+// The same bounded wait, inlined at the call site: for waits on the
+// output path with many live registers (no call, so nothing is saved to and
+// reloaded from the stack around it).
+__device__ __forceinline__ bool mbar_wait_inline(uint32_t bar, uint32_t parity, const WaitGuard& g,
+                                                 uint32_t code, bool honour_abort) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 31u) == 0) {
+            if (honour_abort && *g.abort) return false;
+            if (globaltimer_ns() - t0 > g.timeout_ns) {
+                *g.abort = 1u;
+                report_timeout(g.err_word, g.err_host, code);
+                return false;
+            }
+        }
+    }
+}
+
 // Teardown variant: ignores the abort flag (used to drain copies or MMAs
 // that are still in flight before shared/tensor memory is released).
 __device__ __forceinline__ bool mbar_drain(uint32_t bar, uint32_t parity, const WaitGuard& g,

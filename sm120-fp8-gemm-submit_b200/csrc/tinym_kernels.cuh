@@ -408,7 +408,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint64_t db0 = sw128_kmajor_desc(x_ring);
         int s = 0;
         uint32_t ph = 0u;
-        for (int i = 0; i < nkb; ++i) {
+        int i = 0;
+        for (; i < nkb; ++i) {
             bool ok = true;
             if (lane == 0) ok = mbar_wait_inline(full_bar(s), ph, guard, kErrMmaWait, true);
             if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) break;
@@ -428,7 +429,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                   kIdesc, (c | kk) ? 1u : acc0);
                     }
                 }
-                umma_commit(empty_bar(s));  // frees the slot once these MMAs retire
+                // frees the slot once these MMAs retire; the last stage's
+                // commit completes the accumulator instead
+                umma_commit(i < nkb - 1 ? empty_bar(s) : acc_bar);
             }
             __syncwarp();
             if (++s == stages) {
@@ -437,7 +440,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
         }
         if (lane == 0) {
-            umma_commit(acc_bar);  // accumulator complete (or all issued MMAs retired)
+            // after an abort: every issued MMA retired
+            if (i < nkb) umma_commit(acc_bar);
             if (*abort_flag) mbar_drain(acc_bar, 0, guard, kErrDrain);
             // Free TMEM as soon as every epilogue warp has read it (each
             // arrives even without an accumulator), off the output path.
@@ -560,7 +564,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // and stores them straight from registers (for each m, the lanes of a
     // warp write consecutive N: one coalesced segment per warp and m).
     if (threadIdx.x == 64) TINYM_TRACE(15);
-    if (have_acc && row_mine && !*abort_flag) {
+    if (have_acc && row_mine) {
         const int n = tile * TILE_M + row;
         if (n < p.n) {
             // Destinations: y, or this rank's column block of every rank's

@@ -372,8 +372,8 @@ constexpr uint32_t kFlagQuantPrologue = 1u << 16;
 // stream W during its tail: measured 4-9 % more back-to-back throughput at
 // M = 9 on the official points.
 constexpr int kOverlapRingBytes = 64 * 1024;
-// W in flight per CTA for the 64-row full-K plans (fewer, longer-lived CTAs).
-constexpr int kFullKRingBytes = 160 * 1024;
+// W in flight per CTA for plans with 64 KiB stages (block_k = 512).
+constexpr int kWideRingBytes = 192 * 1024;
 constexpr uint32_t kHalfSmSmem = (233472u - 2u * 1024u) / 2u;  // two CTAs' share of an SM
 
 // Ring depth for a TC plan: ring_bytes of W in flight, at most what fits
@@ -392,20 +392,15 @@ int tc_stages_for(const tinym_plan& p, int64_t kb_per_cta, int ring_bytes = kTar
 //  * block_k = 256 -- one 32 KiB 3-D TMA box of W per stage -- whenever
 //    K % 128 == 0, else 128.  A CTA's TMA stream costs ~150 ns per box
 //    whatever its size up to 32 KiB (54 GB/s per CTA with 8 KiB boxes, 106
-//    with 16 KiB, ~150-190 with 32 KiB, measured with few CTAs), while
-//    64 KiB stages lengthen the tensor core's drain of the last stage and
-//    the start-up; 32 KiB x 4 stages measured best at every official point;
+//    with 16 KiB, ~150-190 with 32 KiB, measured with few CTAs);
 //  * 128-row W tiles and the largest K split (cluster size <= 8) that keeps
 //    tiles * split CTAs within one CTA per SM and gives every CTA >= 2
 //    stages, with a ring of ~128 KiB of W (tc_stages_for);
-//  * except for M > 8 when that split is 3 or more and there are enough
-//    64-row tiles to keep about half of the SMs streaming (e.g. N = 5120):
-//    64-row tiles with full K, one 32 KiB box of 64 rows x 512 B per stage
-//    and a ~160 KiB ring, no reduction -- 0.25-0.3 us faster back to back
-//    at (9..16, 6144, 5120) and the same per single launch.  For M <= 8 the
-//    two are equal back to back and the split plan is ~0.2 us faster per
-//    single launch; at N = 8192 (split 2) the split plan wins single
-//    launches by ~0.3 us.
+//  * block_k = 512 instead (one 64 KiB box of 128 rows x 512 B per stage,
+//    a ~192 KiB ring) when K % 512 == 0 and every CTA of that split keeps
+//    at least four such stages: 0.3 us faster back to back and 0.25-0.5 us
+//    per single launch at (1..16, 6144, 5120) than 32 KiB stages (and than
+//    64-row tiles with full K), the same at N = 8192 and 16384.
 // overlap = true: the TINYM_FLAG_STATIC_W variant (two CTAs per SM).
 tinym_plan heuristic_plan(int64_t m, int64_t n, int64_t k, int sm_count, bool overlap = false) {
     tinym_plan p{};
@@ -433,15 +428,15 @@ tinym_plan heuristic_plan(int64_t m, int64_t n, int64_t k, int sm_count, bool ov
         p.split_k = s;
     }
     p.stages = tc_stages_for(p, (kb + p.split_k - 1) / p.split_k, ring);
-    if (!overlap && m > 8 && p.split_k >= 3 && k % kBlockK == 0) {
+    if (!overlap && k % (4 * kBlockK) == 0) {
+        // 64 KiB stages (one 3-D box of 128 rows x 512 B) when every CTA of
+        // the split keeps at least four of them.
         tinym_plan q = p;
-        q.tile_m = 64;
-        q.split_k = 1;
         q.block_k = 4 * kBlockK;
-        const int64_t tiles64 = (n + q.tile_m - 1) / q.tile_m;
-        const int64_t kb64 = (k + q.block_k - 1) / q.block_k;
-        const int st = tc_stages_for(q, kb64, kFullKRingBytes);
-        if (tiles64 <= slots && 2 * tiles64 >= slots && kb64 >= 4 && st >= 4) {
+        const int64_t kb4 = k / q.block_k;
+        const int64_t per4 = (kb4 + q.split_k - 1) / q.split_k;
+        const int st = tc_stages_for(q, per4, kWideRingBytes);
+        if (per4 >= 4 && (q.split_k - 1) * per4 < kb4 && st >= 3) {
             q.stages = st;
             p = q;
         }
@@ -678,7 +673,8 @@ static int gemm_prepare(const void* x, const void* w, void* y, int64_t ldy, int6
                 --p.split_k;
             } while (p.split_k > 1 && (p.split_k - 1) * ((kb + p.split_k - 1) / p.split_k) >= kb);
             const int s2 = p.kernel == TINYM_KERNEL_TC
-                               ? tc_stages_for(p, (kb + p.split_k - 1) / p.split_k, ring)
+                               ? tc_stages_for(p, (kb + p.split_k - 1) / p.split_k,
+                                               p.block_k == 4 * kBlockK ? kWideRingBytes : ring)
                                : p.stages;
             if (s2 > 0) p.stages = s2;
             if ((st = fill_derived(m, n, k, &p)) != TINYM_OK) return st;

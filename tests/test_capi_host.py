@@ -132,14 +132,14 @@ def test_zero_plan_fields_mean_defaults():
 
 
 def test_dispatch_tiles_for_official_points():
-    """The measured winners on B200: 128-row tiles, 32 KiB stages four deep,
-    K split 3 / 2 / 1 for N = 5120 / 8192 / 16384; for M > 8 at N = 5120,
-    64-row tiles with full K, 64 rows x 512 B stages five deep."""
+    """The measured winners on B200: 128-row tiles, 64 KiB stages (128 rows x
+    512 B) three deep, K split 3 / 2 / 1 for N = 5120 / 8192 / 16384; 32 KiB
+    stages four deep where a CTA would keep fewer than four 64 KiB stages."""
     import tinym_b200 as t
 
     for m in (1, 8, 9, 16):
-        for k, n, want in ((6144, 5120, (128, 3, 256, 4) if m <= 8 else (64, 1, 512, 5)),
-                           (5120, 8192, (128, 2, 256, 4)), (5120, 16384, (128, 1, 256, 4))):
+        for k, n, want in ((6144, 5120, (128, 3, 512, 3)), (5120, 8192, (128, 2, 512, 3)),
+                           (5120, 16384, (128, 1, 512, 3)), (5120, 4096, (128, 4, 256, 4))):
             p = t.select_plan(m, n, k, 148)
             assert (p.tile_m, p.split_k, p.block_k, p.stages) == want, p.as_dict()
 
@@ -380,4 +380,4 @@ def test_plain_c_caller(tmp_path):
     assert run.returncode == 0, run.stderr
     lines = run.stdout.strip().splitlines()
     assert lines[-1] == "c abi host checks ok"
-    assert "M=9 K=6144 N=5120 split=1 stages=5 block_k=512 tile_m=64 ctas=80" in lines
+    assert "M=9 K=6144 N=5120 split=3 stages=3 block_k=512 tile_m=128 ctas=120" in lines

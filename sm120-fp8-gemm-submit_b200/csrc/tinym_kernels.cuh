@@ -439,9 +439,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 ph ^= 1u;
             }
         }
+        if (i < nkb) {
+            // An abort: the accumulator barrier completes once every MMA
+            // issued so far has retired (committed by the lane that issued
+            // them, as in the loop).
+            if (elect_one()) umma_commit(acc_bar);
+            __syncwarp();
+        }
         if (lane == 0) {
-            // after an abort: every issued MMA retired
-            if (i < nkb) umma_commit(acc_bar);
             if (*abort_flag) mbar_drain(acc_bar, 0, guard, kErrDrain);
             // Free TMEM as soon as every epilogue warp has read it (each
             // arrives even without an accumulator), off the output path.

@@ -499,7 +499,7 @@ def measure_point(m, k, n, device, l2, peak, *, cublas=True, w_dist="normal", la
     stream = torch.cuda.current_stream(device).cuda_stream
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     out = {"M": m, "K": k, "N": n, "w_dist": w_dist,
-           "plan": tinym_b200.select_plan(m, n, k, sms).as_dict()}
+           "plan": tinym_b200.launch_plan(m, n, k).as_dict()}
     impls = [("", ours)] + ([("cublas_", cublas_fn)] if cublas else [])
     if m == 1:
         # the CUDA-core M = 1 kernel beside the tensor-core one (same grid
@@ -643,7 +643,7 @@ def main():
     sets = make_operands(m, k, n_local, n_sets, device, seed=17 + rank)
     stream = torch.cuda.current_stream(device)
     sm_count = torch.cuda.get_device_properties(device).multi_processor_count
-    plan = tinym_b200.select_plan(m, n_local, k, sm_count)
+    plan = tinym_b200.launch_plan(m, n_local, k)  # the plan the launch runs on this GPU
     explicit = None
     if args.plan and args.plan.startswith("simt:"):
         sp, st, cw = (int(v) for v in args.plan[5:].split(","))
@@ -734,7 +734,7 @@ def main():
             side = (f"{other}_scaling",
                     {"N": n_s_total, "n_per_gpu": n_s, "us_per_launch": round(s_us, 3),
                      "aggregate_gbs": round(algo_bytes(m, k, n_s) * world / (s_us * 1e-6) / 1e9, 1),
-                     "plan": tinym_b200.select_plan(m, n_s, k, sm_count).as_dict(),
+                     "plan": tinym_b200.launch_plan(m, n_s, k).as_dict(),
                      "protocol": "median over CUDA-graph replays of back-to-back launches, "
                                  "cold W (rotating buffers), max over ranks"})
             del ss_sets

@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define TINYM_ABI_VERSION 7
+#define TINYM_ABI_VERSION 8
 
 /* Exported-symbol marker (the library is built with hidden visibility). */
 #if defined(__GNUC__)
@@ -148,6 +148,18 @@ TINYM_API int tinym_check_plan(int64_t m, int64_t n, int64_t k, tinym_plan* plan
  * include/fp8_gemm_tinym.cuh:757-766). */
 TINYM_API int tinym_plan_max_active_clusters(int64_t m, int64_t n, int64_t k,
                                              const tinym_plan* plan, int32_t* out);
+
+/* The plan a call with no explicit plan runs on the current device, with
+ * these flags (0 or TINYM_FLAG_STATIC_W): the dispatch table's plan, then
+ * split_k lowered (as the launcher does) until every cluster of the grid
+ * is resident at once, to the next split that still gives every CTA some
+ * K.  Equal to tinym_select_plan_ex(..., device SM count, ...) whenever the
+ * device holds that plan's clusters.  Queries the device (occupancy
+ * calculator); launches nothing.  No reference counterpart (the reference
+ * picks one of six compile-time configurations,
+ * src/torch_candidate_extension.cu:60-78). */
+TINYM_API int tinym_launch_plan(int64_t m, int64_t n, int64_t k, uint32_t flags,
+                                tinym_plan* out);
 
 /* Device error word of the current device: bit flags set by kernels whose
  * bounded waits expired (0 = none).  Synchronises the device.  clear != 0

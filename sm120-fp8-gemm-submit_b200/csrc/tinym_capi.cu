@@ -615,6 +615,39 @@ int tinym_select_plan(int64_t m, int64_t n, int64_t k, int32_t sm_count, tinym_p
     return fill_derived(m, n, k, out);
 }
 
+// The dispatch table's plan as a launch on device `dev` runs it: the
+// heuristic plan, then -- since the table assumes every cluster of the grid
+// is resident at once -- the K split lowered until the device confirms that
+// it is, to the next split that still gives every CTA some K.  The
+// static-W plan (overlap) is built to stream more, smaller CTAs than fit
+// one wave (clusters are independent, so that is correct) and is left as
+// chosen: measured faster than any shrunken variant.
+static int device_table_plan(int64_t m, int64_t n, int64_t k, bool overlap, int dev, DeviceInfo* di,
+                             tinym_plan* out) {
+    tinym_plan p = heuristic_plan(m, n, k, di->sm_count, overlap);
+    int st = fill_derived(m, n, k, &p);
+    if (st != TINYM_OK) return st;
+    const int ring = overlap ? kOverlapRingBytes : kTargetRingBytes;
+    while (!overlap && p.split_k > 1) {
+        int clusters = 0;
+        if ((st = max_active_clusters(p, dev, di, &clusters)) != TINYM_OK) return st;
+        if (clusters >= p.tiles_n) break;
+        // e.g. 20 K blocks: 7 -> 5, since a split of 6 leaves rank 5 nothing
+        const int64_t kb = (k + p.block_k - 1) / p.block_k;
+        do {
+            --p.split_k;
+        } while (p.split_k > 1 && (p.split_k - 1) * ((kb + p.split_k - 1) / p.split_k) >= kb);
+        const int s2 = p.kernel == TINYM_KERNEL_TC
+                           ? tc_stages_for(p, (kb + p.split_k - 1) / p.split_k,
+                                           p.block_k == 4 * kBlockK ? kWideRingBytes : ring)
+                           : p.stages;
+        if (s2 > 0) p.stages = s2;
+        if ((st = fill_derived(m, n, k, &p)) != TINYM_OK) return st;
+    }
+    *out = p;
+    return TINYM_OK;
+}
+
 // Everything one GEMM launch needs, built and validated by gemm_prepare
 // before anything is queued on the stream (the fused activation path
 // validates the GEMM before it launches its prologue).
@@ -653,32 +686,7 @@ static int gemm_prepare(const void* x, const void* w, void* y, int64_t ldy, int6
         if ((st = fill_derived(m, n, k, &p)) != TINYM_OK) return st;
     } else {
         const bool overlap = (flags & tinym::kFlagEarlyW) && !(flags & kFlagQuantPrologue);
-        p = heuristic_plan(m, n, k, di->sm_count, overlap);
-        if ((st = fill_derived(m, n, k, &p)) != TINYM_OK) return st;
-        const int ring = overlap ? kOverlapRingBytes : kTargetRingBytes;
-        // The default table assumes every cluster of the grid is resident at
-        // once; shrink the K split until the device confirms that it is.  The
-        // static-W plan is built to stream more, smaller CTAs than fit one
-        // wave (clusters are independent, so that is correct) and is left
-        // as chosen: measured faster than any shrunken variant.
-        while (!overlap && p.split_k > 1) {
-            int clusters = 0;
-            if ((st = max_active_clusters(p, dev, di, &clusters)) != TINYM_OK) return st;
-            if (clusters >= p.tiles_n) break;
-            // The next smaller split that leaves no CTA an empty K range
-            // (e.g. 20 K blocks: 7 -> 5, since a split of 6 leaves rank 5
-            // nothing).
-            const int64_t kb = (k + p.block_k - 1) / p.block_k;
-            do {
-                --p.split_k;
-            } while (p.split_k > 1 && (p.split_k - 1) * ((kb + p.split_k - 1) / p.split_k) >= kb);
-            const int s2 = p.kernel == TINYM_KERNEL_TC
-                               ? tc_stages_for(p, (kb + p.split_k - 1) / p.split_k,
-                                               p.block_k == 4 * kBlockK ? kWideRingBytes : ring)
-                               : p.stages;
-            if (s2 > 0) p.stages = s2;
-            if ((st = fill_derived(m, n, k, &p)) != TINYM_OK) return st;
-        }
+        if ((st = device_table_plan(m, n, k, overlap, dev, di, &p)) != TINYM_OK) return st;
     }
 
     if (w_packed && p.kernel != TINYM_KERNEL_TC)
@@ -776,6 +784,21 @@ int tinym_select_plan_ex(int64_t m, int64_t n, int64_t k, int32_t sm_count, uint
     if (st != TINYM_OK) return st;
     *out = heuristic_plan(m, n, k, sm_count, (flags & TINYM_FLAG_STATIC_W) != 0);
     return fill_derived(m, n, k, out);
+}
+
+int tinym_launch_plan(int64_t m, int64_t n, int64_t k, uint32_t flags, tinym_plan* out) {
+    t_last_error[0] = '\0';
+    if (!out) return fail(TINYM_ERR_INVALID_ARGUMENT, "out is NULL");
+    if (flags & ~static_cast<uint32_t>(TINYM_FLAG_STATIC_W))
+        return fail(TINYM_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
+    int st = check_shape(m, n, k);
+    if (st != TINYM_OK) return st;
+    int dev = 0;
+    const cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    DeviceInfo* di = nullptr;
+    if ((st = device_info(dev, &di)) != TINYM_OK) return st;
+    return device_table_plan(m, n, k, (flags & TINYM_FLAG_STATIC_W) != 0, dev, di, out);
 }
 
 int tinym_fp8_gemm_ex2(const void* x, const void* w, void* y, int64_t ldy, int64_t m, int64_t n,

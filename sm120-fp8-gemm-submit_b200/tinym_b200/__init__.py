@@ -53,6 +53,7 @@ EXPORTED = (
     "tinym_device_status",
     "tinym_pending_errors",
     "tinym_plan_max_active_clusters",
+    "tinym_launch_plan",
     "tinym_selftest_wait_timeout",
     "tinym_packed_weight_bytes",
     "tinym_pack_weights",
@@ -160,6 +161,8 @@ def capi() -> ctypes.CDLL:
             lib.tinym_plan_max_active_clusters.argtypes = [i64, i64, i64, ctypes.POINTER(Plan),
                                                            ctypes.POINTER(ctypes.c_int32)]
             lib.tinym_plan_max_active_clusters.restype = ctypes.c_int
+            lib.tinym_launch_plan.argtypes = [i64, i64, i64, ctypes.c_uint32, ctypes.POINTER(Plan)]
+            lib.tinym_launch_plan.restype = ctypes.c_int
             lib.tinym_packed_weight_bytes.argtypes = [i64, i64, ctypes.POINTER(i64)]
             lib.tinym_packed_weight_bytes.restype = ctypes.c_int
             lib.tinym_pack_weights.argtypes = [vp, vp, i64, i64, vp]
@@ -395,6 +398,15 @@ def gemm_allgather_ptr(x_ptr: int, w_ptr: int, m: int, n_local: int, k: int, des
     pl = ctypes.byref(plan) if plan is not None else None
     _check(capi().tinym_fp8_gemm_allgather(x_ptr, w_ptr, m, n_local, k, alpha_ptr, alpha,
                                            ctypes.byref(desc), pl, stream))
+
+
+def launch_plan(m: int, n: int, k: int, static_w: bool = False) -> Plan:
+    """The plan a call without an explicit plan runs on the current GPU:
+    the dispatch table's choice with the K split lowered, as the launcher
+    does, until every cluster is resident at once (queries the device)."""
+    p = Plan()
+    _check(capi().tinym_launch_plan(m, n, k, 1 if static_w else 0, ctypes.byref(p)))
+    return p
 
 
 def max_active_clusters(m: int, n: int, k: int, plan: Plan) -> int:

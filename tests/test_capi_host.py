@@ -33,7 +33,7 @@ def test_library_exports_every_declared_symbol():
     lib = tinym_b200.capi()
     for name in declared_symbols():
         assert hasattr(lib, name), name
-    assert lib.tinym_abi_version() == 7
+    assert lib.tinym_abi_version() == 8
 
 
 def test_status_strings():

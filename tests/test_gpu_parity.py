@@ -156,6 +156,31 @@ def test_sharded_slab_shapes(cuda_device, oracle, m, k, n):
     _check(oracle, out, xq, wq, alpha)
 
 
+@pytest.mark.parametrize("m,k,n", [(9, 5120, 2048), (1, 6144, 5120), (9, 5120, 16384)])
+def test_launch_plan_is_what_runs(cuda_device, oracle, m, k, n):
+    """tinym_launch_plan reports the plan a call without a plan runs: the
+    table's plan, with the K split lowered where the device cannot hold
+    every cluster; running it explicitly gives the same bits."""
+    import torch
+
+    import tinym_b200
+
+    sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
+    table = tinym_b200.select_plan(m, n, k, sms)
+    lp = tinym_b200.launch_plan(m, n, k)
+    assert lp.split_k <= table.split_k and lp.block_k == table.block_k
+    assert tinym_b200.max_active_clusters(m, n, k, lp) >= lp.tiles_n
+    if tinym_b200.max_active_clusters(m, n, k, table) >= table.tiles_n:
+        assert lp.as_dict() == table.as_dict()
+    xq, wq, sx, sw, alpha = oracle.make_case(m, k, n, seed=m + n, dist="normal")
+    x, w = _to_dev(xq, cuda_device), _to_dev(wq, cuda_device)
+    a = torch.from_numpy(alpha).to(cuda_device)
+    y_default = _run(x, w, a)
+    y_plan = _run(x, w, a, plan=lp)
+    assert torch.equal(y_default, y_plan)
+    _check(oracle, y_default, xq, wq, alpha)
+
+
 def _valid(tinym_b200, m, k, n, plan):
     try:
         tinym_b200.check_plan(m, n, k, plan)

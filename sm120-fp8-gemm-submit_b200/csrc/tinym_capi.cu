@@ -653,6 +653,7 @@ static int device_table_plan(int64_t m, int64_t n, int64_t k, bool overlap, int 
 // validates the GEMM before it launches its prologue).
 struct GemmLaunch {
     CUtensorMap tm_w, tm_x;  // 64-byte aligned by their type
+    CUtensorMap tm_w1;       // TC kernel: W one 128-byte K chunk per box (its last stage)
     TinymParams prm;
     tinym_plan plan;
     const void* fn;
@@ -698,6 +699,10 @@ static int gemm_prepare(const void* x, const void* w, void* y, int64_t ldy, int6
         return st;
     if (p.kernel == TINYM_KERNEL_TC) {
         if ((st = get_map(x, m, k, p.mma_n, 1, chunks, dev, &out->tm_x)) != TINYM_OK) return st;
+        out->tm_w1 = out->tm_w;
+        if (chunks > 1 &&
+            (st = get_map(w, n, k, p.tile_m, 1, 1, dev, &out->tm_w1, w_packed ? 1 : 0)) != TINYM_OK)
+            return st;
     } else {
         if ((st = get_map(x, m, k, 1, 0, 1, dev, &out->tm_x)) != TINYM_OK) return st;
     }
@@ -748,8 +753,10 @@ static int gemm_launch(GemmLaunch& g, void* stream) {
     cudaLaunchConfig_t cfg{};
     cudaLaunchAttribute attrs[2];
     launch_config(g.plan, stream, &cfg, attrs);
-    void* args[3] = {&g.tm_w, &g.tm_x, &g.prm};
-    const cudaError_t e = cudaLaunchKernelExC(&cfg, g.fn, args);
+    void* tc_args[4] = {&g.tm_w, &g.tm_x, &g.tm_w1, &g.prm};
+    void* simt_args[3] = {&g.tm_w, &g.tm_x, &g.prm};
+    const cudaError_t e =
+        cudaLaunchKernelExC(&cfg, g.fn, g.plan.kernel == TINYM_KERNEL_TC ? tc_args : simt_args);
     if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
     return TINYM_OK;
 }

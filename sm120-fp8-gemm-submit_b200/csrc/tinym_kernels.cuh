@@ -149,7 +149,9 @@ __host__ __device__ inline SmemLayout smem_layout(int stages, int w_stage_bytes,
     L.red_off = (L.red_off + 15u) & ~15u;
     const uint32_t red_bytes = static_cast<uint32_t>((split - 1) * red_rank_bytes);
     L.bar_off = (L.red_off + red_bytes + 7u) & ~7u;
-    L.misc_off = L.bar_off + static_cast<uint32_t>(2 * stages + 3) * 8u;
+    // barriers: full and empty per stage, accumulator, reduction, TMEM
+    // release, and up to three chunk barriers of the TC kernel's last stage
+    L.misc_off = L.bar_off + static_cast<uint32_t>(2 * stages + 6) * 8u;
     // +1024: the dynamic window is re-aligned to 1024 bytes in the kernel.
     L.bytes = L.misc_off + 16u + 1024u;
     return L;
@@ -200,7 +202,8 @@ __device__ __forceinline__ float load_alpha(const TinymParams& p) {
 template <int MMA_N, int CHUNKS, int TILE_M>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tinym_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
-                    const __grid_constant__ CUtensorMap tm_x, const TinymParams p) {
+                    const __grid_constant__ CUtensorMap tm_x,
+                    const __grid_constant__ CUtensorMap tm_w1, const TinymParams p) {
     static_assert(MMA_N == 8 || MMA_N == 16, "MMA_N must be 8 or 16");
     static_assert(CHUNKS == 1 || CHUNKS == 2 || CHUNKS == 4, "1, 2 or 4 K chunks per stage");
     static_assert(TILE_M == 64 || TILE_M == 128, "W tiles of 64 or 128 rows (MMA M)");
@@ -240,6 +243,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // One arrive per epilogue warp once its accumulator reads are complete:
     // the MMA warp then frees TMEM while the epilogue is still running.
     const uint32_t tmem_bar = bars + 8u * (2 * stages + 2);
+    // The CTA's last stage (CHUNKS > 1) is loaded one 128-byte K chunk per box
+    // (tm_w1): chunk 0 and X complete on the stage's full barrier, chunk c on
+    // tail_bar(c), so the MMAs of the first chunks run while later ones land.
+    auto tail_bar = [&](int c) { return bars + 8u * (2 * stages + 2 + c); };
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.misc_off);
     volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L.misc_off + 4);
     // Partial sums from the other ranks land in their own region.
@@ -274,8 +281,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // Stage i of this CTA's K range goes to ring slot s (= i mod stages; the
     // loops below keep s and the slot's phase parity in running counters,
     // since a runtime division per stage measurably slows the issue loops).
+    // K chunks of this CTA's last stage that lie inside K (K % 128 == 0
+    // whenever CHUNKS > 1); the others carry no data and get no MMA.
+    const int last_chunks = min(CHUNKS, p.k / kBlockK - (kb0 + nkb - 1) * CHUNKS);
     auto issue_w = [&](int i, int s) {
         const int chunk = (kb0 + i) * CHUNKS;  // first 128-byte K chunk of the stage
+        if constexpr (CHUNKS > 1) {
+            if (i == nkb - 1) {
+                mbar_expect_tx(full_bar(s), static_cast<uint32_t>(kWChunk + kXStageBytes));
+                for (int c = 0; c < last_chunks; ++c) {
+                    const uint32_t bar = c == 0 ? full_bar(s) : tail_bar(c);
+                    if (c > 0) mbar_expect_tx(bar, static_cast<uint32_t>(kWChunk));
+                    const uint32_t dst = w_ring + s * kWStage + c * kWChunk;
+                    if (p.w_packed_kc) {
+                        const int r0 = tile * TILE_M;
+                        tma_load_3d(dst, &tm_w1, bar, 0, r0 % kPackRows,
+                                    (r0 / kPackRows) * p.w_packed_kc + chunk + c, pol_w);
+                    } else {
+                        tma_load_2d(dst, &tm_w1, bar, (chunk + c) * kBlockK, tile * TILE_M, pol_w);
+                    }
+                }
+                return;
+            }
+        }
         mbar_expect_tx(full_bar(s), kStageTx);
         if (p.w_packed_kc) {
             const int r0 = tile * TILE_M;
@@ -308,6 +336,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // the full barriers are initialised (and published to the async
         // proxy) ahead of it; the other barriers follow while it is in flight.
         for (int s = 0; s < stages; ++s) mbar_init(full_bar(s), 1);
+        if constexpr (CHUNKS > 1)
+            for (int c = 1; c < CHUNKS; ++c) mbar_init(tail_bar(c), 1);
         fence_mbar_init();
         fence_proxy_async_smem();
         TINYM_TRACE(10);
@@ -395,6 +425,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 // Drain the copies still in flight before shared memory is released.
                 for (int j = max(0, issued - stages); j < issued; ++j)
                     mbar_drain(full_bar(j % stages), (j / stages) & 1, guard, kErrDrain);
+                if (CHUNKS > 1 && issued == nkb)
+                    for (int c = 1; c < last_chunks; ++c) mbar_drain(tail_bar(c), 0, guard, kErrDrain);
             }
         }
     } else if (warp == 1) {
@@ -419,9 +451,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint64_t da = da0 + static_cast<uint64_t>((s * kWStage) >> 4);
             const uint64_t db = db0 + static_cast<uint64_t>((s * kXStageBytes) >> 4);
             const uint32_t acc0 = i > 0 ? 1u : 0u;  // the CTA's first MMA overwrites D
+            const bool split_last = CHUNKS > 1 && i == nkb - 1;
             if (elect_one()) {
 #pragma unroll
                 for (int c = 0; c < CHUNKS; ++c) {
+                    if (split_last && c > 0) {
+                        if (c >= last_chunks) break;
+                        if (!mbar_wait_inline(tail_bar(c), 0u, guard, kErrMmaWait, true)) break;
+                        tc_fence_after_sync();
+                    }
 #pragma unroll
                     for (int kk = 0; kk < kBlockK / 32; ++kk) {
                         umma_e4m3(tmem_u, da + static_cast<uint64_t>((c * kWChunk + kk * 32) >> 4),

@@ -12,7 +12,8 @@
 //    boundary (the 128-byte swizzle atom the tcgen05 descriptors assume),
 //    the split-K receive blocks are 16-byte aligned for st.async v4, the
 //    mbarriers 8-byte aligned with room for the last stage's chunk
-//    barriers, and the whole carve-up matches the size the host requests;
+//    barriers, and the whole carve-up matches the size the host requests
+//    (the CUDA-core M = 1 kernel's carve-up as well);
 //  * K ranges of a cluster: with the plan check's rule every rank gets at
 //    least one K stage, and the last stage's in-range chunk count (the
 //    chunked last stage of the TC kernel) lies in [1, chunks].
@@ -139,6 +140,30 @@ void check_k_ranges() {
     }
 }
 
+// The CUDA-core M = 1 kernel: 128-row W stages (128-byte swizzle) and one
+// unswizzled 128-byte X row per stage; split-K partials of 128 FP32 rows per
+// sending rank land in rank 0's receive region.
+void check_simt_layout() {
+    for (int split = 1; split <= tinym::kMaxSplit; ++split)
+        for (int stages = 2; stages <= 32; ++stages) {
+            const int x_stage = tinym::kBlockK;
+            const int red_rank = tinym::kTileRows * 4;
+            const tinym::SmemLayout L =
+                tinym::smem_layout(stages, tinym::kWStageBytes, x_stage, split, red_rank);
+            expect(L.w_off % 1024 == 0 && tinym::kWStageBytes % 1024 == 0,
+                   "SIMT W stages on 1024-byte boundaries", split, stages, 0, 0);
+            expect(L.x_off % 128 == 0 && x_stage % 128 == 0,
+                   "SIMT X rows on 128-byte boundaries", split, stages, 0, 0);
+            expect(L.red_off % 16 == 0 && red_rank % 16 == 0 &&
+                       L.red_off >= L.x_off + static_cast<uint32_t>(stages * x_stage),
+                   "SIMT receive region 16-byte aligned after the X ring", split, stages, 0, 0);
+            expect(L.bar_off % 8 == 0 &&
+                       L.bar_off >= L.red_off + static_cast<uint32_t>((split - 1) * red_rank) &&
+                       L.bar_off + 8u * (2u * stages + 2u) <= L.misc_off,
+                   "SIMT mbarriers 8-byte aligned with room for every stage", split, stages, 0, 0);
+        }
+}
+
 void check_packed_chunks() {
     for (int64_t k = 16; k <= 16384; k += 16) {
         const int64_t kc = tinym::packed_chunks(k);
@@ -154,6 +179,7 @@ void check_packed_chunks() {
 int main() {
     check_row_ownership();
     check_tc_layout();
+    check_simt_layout();
     check_k_ranges();
     check_packed_chunks();
     if (g_failures) {

@@ -393,7 +393,21 @@ class near_gpu:
 
 
 def cpu_baseline(m, k, n, budget_s=10.0):
-    """The oracle on this host's cores: a bounded number of full GEMMs."""
+    """The oracle on this host's cores: a bounded number of full GEMMs, with
+    the BLAS thread pool opened to every CPU this process may run on (torchrun
+    sets OMP_NUM_THREADS=1 for each rank, which would leave the reference arm
+    at N > 1 on one thread)."""
+    import numpy as np  # noqa: F401  (its BLAS must be loaded for the limit to reach it)
+
+    try:
+        from threadpoolctl import threadpool_limits
+    except ImportError:
+        return _cpu_baseline(m, k, n, budget_s)
+    with threadpool_limits(limits=len(os.sched_getaffinity(0)) or 1):
+        return _cpu_baseline(m, k, n, budget_s)
+
+
+def _cpu_baseline(m, k, n, budget_s):
     import numpy as np
 
     from oracle import fp8_oracle as orc

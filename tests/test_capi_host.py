@@ -307,15 +307,18 @@ def test_ipc_export_rejects_null_arguments():
 
 def test_bench_reference_arm_prints_one_line():
     """The driver's reference arm: the CPU oracle on the host cores, one JSON
-    line with the contract's keys."""
+    line with the contract's keys.  Run with OMP_NUM_THREADS=1, as torchrun
+    sets it for every rank: the arm still uses every CPU it may run on."""
     import json
+    import os
     import subprocess
     import sys
 
     root = Path(__file__).resolve().parents[1]
+    env = dict(os.environ, OMP_NUM_THREADS="1")
     res = subprocess.run([sys.executable, str(root / "bench.py"), "--impl", "reference",
                           "--steps", "1", "--warmup", "3"],
-                         capture_output=True, text=True, timeout=240, cwd=root)
+                         capture_output=True, text=True, timeout=240, cwd=root, env=env)
     assert res.returncode == 0, res.stderr[-2000:]
     lines = [ln for ln in res.stdout.strip().splitlines() if ln.strip()]
     assert len(lines) == 1
@@ -323,6 +326,7 @@ def test_bench_reference_arm_prints_one_line():
     assert d["impl"] == "reference" and d["unit"] == "GB/s" and d["value"] > 0
     assert d["cpu_baseline"]["kind"] in ("port", "reference")
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["gpu_launches"] == 0
+    assert d["cpu_baseline"]["cores"] == len(os.sched_getaffinity(0))
 
 
 def test_torch_wrappers_validate_before_launch():

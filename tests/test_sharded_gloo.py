@@ -147,6 +147,79 @@ def test_fused_gather_refused_on_every_rank_when_n_below_world():
     assert res == [(0, "refused"), (1, "refused")]
 
 
+def _worker_rank_leaves(rank, world, port, q):
+    """One gathered call on every rank, then rank 1 leaves between steps (the
+    process ends with nothing in flight) while rank 0 makes the next call."""
+    import datetime
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    outcome = "no result"
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=10))
+        import sys
+        from pathlib import Path
+
+        root = Path(__file__).resolve().parents[1]
+        sys.path.insert(0, str(root / "sm120-fp8-gemm-submit_b200"))
+        from tinym_b200.sharded import ShardedFp8Gemm
+
+        def cpu_gemm(x, w_local, a, out):  # stands in for the kernel
+            out.copy_((x.float() @ w_local.float().t() * a).to(torch.bfloat16))
+            return out
+
+        w = torch.randn(256, 32)
+        x = torch.randn(2, 32)
+        g = ShardedFp8Gemm.from_full_weight(w, local_gemm=cpu_gemm)
+        y = g(x, 1.0)
+        assert tuple(y.shape) == (2, 256)
+        dist.barrier()
+        if rank == 1:
+            outcome = "left"
+        else:
+            time.sleep(1.0)  # rank 1 is gone by now
+            t0 = time.monotonic()
+            try:
+                g(x, 1.0)
+                outcome = "no error"
+            except Exception as e:  # the collective ends with an error
+                outcome = f"error after {time.monotonic() - t0:.1f} s: {type(e).__name__}"
+    except Exception as e:  # pragma: no cover - reported to the parent
+        outcome = repr(e)
+    q.put((rank, outcome))
+    q.close()
+    q.join_thread()
+    os._exit(0)  # no teardown collective with a rank that has left
+
+
+def test_rank_leaving_between_steps_ends_peers_next_gather_with_error():
+    """Failure detection on the host: a rank that leaves between steps makes
+    the next gathered call of the other rank raise (the process group's short
+    timeout or the closed connection) instead of waiting for good."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_rank_leaves, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        if p.exitcode is None:  # pragma: no cover - never expected
+            p.kill()
+        assert p.exitcode == 0
+    assert res[1] == "left", res
+    assert res[0].startswith("error after "), res
+    assert float(res[0].split()[2]) < 30.0, res
+
+
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
 def test_bench_rank_slabs(world):
     """The multi-GPU bench's slab arithmetic: weak scaling keeps every rank's
